@@ -1,0 +1,381 @@
+"""The serving engine of one TP rank: sessions, paged KV, prefill chunks and CUDA-graph decode.
+
+Mirrors the reference ``zip`` engine's execution model (``agent/src/inference/coordinator.rs``):
+a session is prefilled (possibly in several chunks), then joins the decode queue; each decode step
+runs one microbatch of sessions; a session completes after ``max_new_tokens``. The scheduler here
+is prefill-first continuous batching: waiting prompts are prefilled in token-budgeted chunks, and
+running sessions decode together in fixed batch slots.
+
+B200 specifics:
+* KV pages live in one HBM pool per rank (16-token pages); block tables are device tensors, the
+  attention kernels read pages in place (no per-step K/V materialisation as in the reference's
+  ``build_active_tensors``, forward_pass.rs:633-680).
+* Decode steps replay a CUDA graph per batch bucket. Token ids never leave the device between
+  steps: the graph reads and overwrites the same ids buffer; a history buffer keeps every
+  generated token and is copied to the host once per ``sync_every`` steps (or when asked).
+* All ranks of a TP group run the same schedule: rank 0 decides and broadcasts, or (as in the
+  benchmark) every rank receives the same request list and makes the same decisions.
+"""
+from __future__ import annotations
+
+import math
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..models.llama import KVPool, LlamaRunner, StepMeta
+from .pages import PageAllocator
+
+
+@dataclass
+class Session:
+    sid: int
+    prompt: List[int]
+    max_new_tokens: int
+    temperature: float = 0.0
+    top_p: float = 1.0
+    seed_base: int = 0
+    eos_token: Optional[int] = None
+    generated: List[int] = field(default_factory=list)
+    pages: List[int] = field(default_factory=list)
+    kv_len: int = 0            # tokens whose K/V are in the pool
+    prefilled: int = 0         # prompt tokens prefilled so far
+    slot: int = -1             # decode batch slot
+    n_generated: int = 0       # tokens generated (device-side count, known on host)
+    decode_steps_served: int = 0
+    status: str = "waiting"    # waiting | prefilling | decoding | finished
+    t_submit: float = 0.0
+    ttft_event: Optional[torch.cuda.Event] = None
+
+    @property
+    def done(self) -> bool:
+        return self.n_generated >= self.max_new_tokens
+
+
+class DecodeGraphs:
+    """Static decode buffers shared by all buckets plus one captured graph per bucket."""
+
+    def __init__(self, runner: LlamaRunner, max_batch: int, max_pages_per_seq: int, use_graphs: bool,
+                 buckets):
+        dev = runner.device
+        self.runner = runner
+        self.max_batch = max_batch
+        self.ids = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.slot = torch.full((max_batch,), -1, dtype=torch.int64, device=dev)
+        self.seq_lens = torch.ones(max_batch, dtype=torch.int32, device=dev)
+        self.block_tables = torch.zeros(max_batch, max_pages_per_seq, dtype=torch.int32, device=dev)
+        self.max_pages = max_pages_per_seq
+        self.use_graphs = use_graphs
+        self.buckets = [b for b in buckets if b <= max_batch] or [max_batch]
+        if self.buckets[-1] < max_batch:
+            self.buckets.append(max_batch)
+        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: Dict[int, int] = {}
+        self.bufs: Dict[int, dict] = {}
+        self.outs: Dict[int, torch.Tensor] = {}
+        self.pool = None
+
+    def bucket_for(self, n: int) -> int:
+        for b in self.buckets:
+            if n <= b:
+                return b
+        raise ValueError(f"decode batch {n} exceeds max batch {self.max_batch}")
+
+    def meta(self, b: int) -> StepMeta:
+        return StepMeta(ids=self.ids[:b], pos=self.pos[:b], slot=self.slot[:b], block_tables=self.block_tables[:b],
+                        seq_lens=self.seq_lens[:b], max_q_len=self.max_pages * self.runner.kv.page_size,
+                        decode=True)
+
+    def _run(self, b: int):
+        out = self.runner.forward(self.meta(b), self.bufs.setdefault(b, {}))
+        # next ids overwrite the input ids in place (embedding already consumed them)
+        self.ids[:b].copy_(out)
+        return out
+
+    def capture(self, b: int):
+        if b in self.graphs or not self.use_graphs:
+            return
+        # warm-up outside capture sizes the workspaces and sets kernel attributes
+        saved = (self.ids.clone(), self.pos.clone(), self.slot.clone(), self.seq_lens.clone())
+        self.slot[:b].fill_(-1)
+        self._run(b)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        from .. import ops
+        n0 = ops.LAUNCHES[0]
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, pool=self.pool):
+                self._run(b)
+        self.graph_launches[b] = ops.LAUNCHES[0] - n0
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        if self.pool is None:
+            self.pool = g.pool()
+        self.graphs[b] = g
+        self.ids.copy_(saved[0]); self.pos.copy_(saved[1]); self.slot.copy_(saved[2]); self.seq_lens.copy_(saved[3])
+
+    def step(self, b: int):
+        if self.use_graphs:
+            if b not in self.graphs:
+                self.capture(b)
+            self.graphs[b].replay()
+            from .. import ops
+            ops._count(self.graph_launches[b])
+        else:
+            self._run(b)
+
+    def release(self):
+        self.graphs.clear()
+        self.bufs.clear()
+        self.pool = None
+
+
+class Engine:
+    """One rank's engine. All ranks of a TP group must call the same methods in the same order."""
+
+    def __init__(self, runner: LlamaRunner, ecfg: EngineConfig, max_batch: int = 64, sync_every: int = 0,
+                 history_steps: int = 4096):
+        self.runner = runner
+        self.cfg: ModelConfig = runner.cfg
+        self.ecfg = ecfg
+        self.device = runner.device
+        ps = runner.kv.page_size
+        self.page_size = ps
+        self.alloc = PageAllocator(runner.kv.num_pages, reserved=1)
+        self.max_pages_per_seq = (ecfg.max_seq_len + ps - 1) // ps
+        self.dec = DecodeGraphs(runner, max_batch, self.max_pages_per_seq, ecfg.use_cuda_graphs,
+                                ecfg.decode_batch_buckets)
+        self.sessions: Dict[int, Session] = {}
+        self.waiting: deque = deque()
+        self.running: List[Optional[Session]] = [None] * max_batch
+        self.next_sid = 0
+        self.max_batch = max_batch
+        self.sync_every = sync_every
+        # generated-token history: row = decode step, column = batch slot
+        self.history = torch.zeros(history_steps, max_batch, dtype=torch.int32, device=self.device)
+        self.hist_rows: List[List[Optional[int]]] = []   # per row: slot -> sid mapping
+        self.hist_first: List[tuple] = []                # (sid, device tensor idx) of prefill tokens
+        self.prefill_tokens_buf = None
+        self.bt_host = np.zeros((max_batch, self.max_pages_per_seq), dtype=np.int32)
+        self.bt_dirty = True
+        self.steps = 0
+        self.stats = dict(prefill_tokens=0, decode_tokens=0, decode_steps=0, prefill_chunks=0,
+                          peak_batch_size=0)
+
+    # ----------------------------------------------------------------------------- requests
+    def submit(self, prompt: List[int], max_new_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
+               seed_base: int = 0, eos_token: Optional[int] = None) -> int:
+        if not prompt:
+            raise ValueError("Cannot prefill an empty prompt without an explicit BOS policy")
+        if temperature > 0.0:
+            raise NotImplementedError("the CUDA-graph decode path samples greedily; use temperature=0")
+        if len(prompt) + max_new_tokens > self.ecfg.max_seq_len:
+            raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
+                             f"{self.ecfg.max_seq_len}")
+        sid = self.next_sid
+        self.next_sid += 1
+        s = Session(sid, list(prompt), max_new_tokens, temperature, top_p, seed_base, eos_token,
+                    t_submit=time.perf_counter())
+        self.sessions[sid] = s
+        self.waiting.append(s)
+        return sid
+
+    def has_work(self) -> bool:
+        return bool(self.waiting) or any(s is not None for s in self.running)
+
+    # ----------------------------------------------------------------------------- pages
+    def _ensure_pages(self, s: Session, upto_tokens: int):
+        need = (upto_tokens + self.page_size - 1) // self.page_size
+        if need > self.max_pages_per_seq:
+            raise RuntimeError(f"session {s.sid} exceeds {self.max_pages_per_seq} pages")
+        while len(s.pages) < need:
+            p = self.alloc.alloc(1)
+            if p is None:
+                raise RuntimeError("KV page pool exhausted")
+            s.pages.append(p[0])
+            if s.slot >= 0:
+                self.bt_host[s.slot, len(s.pages) - 1] = p[0]
+                self.bt_dirty = True
+
+    def _free_session(self, s: Session):
+        self.alloc.free(s.pages)
+        s.pages = []
+        if s.slot >= 0:
+            self.running[s.slot] = None
+            self.bt_host[s.slot, :] = 0
+            self.bt_dirty = True
+            s.slot = -1
+
+    # ----------------------------------------------------------------------------- prefill
+    def _free_slots(self) -> List[int]:
+        return [i for i, s in enumerate(self.running) if s is None]
+
+    def prefill_step(self, token_budget: Optional[int] = None) -> List[Session]:
+        """Prefill a chunk of waiting prompts (whole prompts or the next piece of a long one)."""
+        budget = token_budget or self.ecfg.prefill_chunk_tokens
+        free = self._free_slots()
+        items = []  # (session, start, end)
+        used = 0
+        while self.waiting and used < budget:
+            s = self.waiting[0]
+            if s.slot < 0:
+                if not free:
+                    break
+            take = min(len(s.prompt) - s.prefilled, budget - used)
+            if take <= 0:
+                break
+            if s.slot < 0:
+                s.slot = free.pop(0)
+                self.running[s.slot] = s
+                s.status = "prefilling"
+            items.append((s, s.prefilled, s.prefilled + take))
+            used += take
+            if s.prefilled + take == len(s.prompt):
+                self.waiting.popleft()
+            else:
+                break  # a partially prefilled prompt ends the chunk
+        if not items:
+            return []
+        dev = self.device
+        ids, pos, slot, cu, klen, last = [], [], [], [0], [], []
+        bt = np.zeros((len(items), self.max_pages_per_seq), dtype=np.int32)
+        for i, (s, a, b) in enumerate(items):
+            self._ensure_pages(s, b)
+            ids.extend(s.prompt[a:b])
+            pr = np.arange(a, b)
+            pos.extend(pr.tolist())
+            pages = np.asarray(s.pages, dtype=np.int64)
+            slot.extend((pages[pr // self.page_size] * self.page_size + pr % self.page_size).tolist())
+            cu.append(cu[-1] + (b - a))
+            klen.append(b)
+            last.append(cu[-1] - 1)
+            bt[i, :len(s.pages)] = s.pages
+            self.bt_host[s.slot, :len(s.pages)] = s.pages
+        self.bt_dirty = True
+        T = len(ids)
+        pin = lambda a, dt: torch.tensor(a, dtype=dt).pin_memory().to(dev, non_blocking=True)
+        m = StepMeta(ids=pin(ids, torch.int32), pos=pin(pos, torch.int32), slot=pin(slot, torch.int64),
+                     block_tables=torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True),
+                     seq_lens=pin(klen, torch.int32), cu_q=pin(cu, torch.int32), last_idx=pin(last, torch.int64),
+                     max_q_len=max(b - a for _, a, b in items), decode=False)
+        next_ids = self.runner.forward(m)
+        finished_prompts = []
+        rows, slots = [], []
+        for i, (s, a, b) in enumerate(items):
+            s.prefilled = b
+            s.kv_len = b
+            if b == len(s.prompt):
+                rows.append(i)
+                slots.append(s.slot)
+                finished_prompts.append(s)
+        if rows:
+            ri = torch.tensor(rows, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            si = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            toks = next_ids.index_select(0, ri)
+            self.dec.ids.index_copy_(0, si, toks)
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            for s in finished_prompts:
+                s.status = "decoding"
+                s.n_generated = 1
+                s.ttft_event = ev
+            self.hist_first.append(([s.sid for s in finished_prompts], toks))
+        self.stats["prefill_tokens"] += T
+        self.stats["prefill_chunks"] += 1
+        for s in finished_prompts:
+            if s.done:
+                self._retire(s)
+        return finished_prompts
+
+    # ----------------------------------------------------------------------------- decode
+    def decode_step(self) -> int:
+        """One decode step over all sessions in the decode phase; returns the batch size."""
+        act = [s for s in self.running if s is not None and s.status == "decoding"]
+        if not act:
+            return 0
+        hi = max(s.slot for s in act) + 1
+        b = self.dec.bucket_for(hi)
+        pos = np.zeros(b, dtype=np.int32)
+        seq = np.ones(b, dtype=np.int32)
+        slot = np.full(b, -1, dtype=np.int64)
+        for s in act:
+            p = s.kv_len  # position of the token being fed
+            self._ensure_pages(s, p + 1)
+            pos[s.slot] = p
+            seq[s.slot] = p + 1
+            slot[s.slot] = s.pages[p // self.page_size] * self.page_size + p % self.page_size
+        d = self.dec
+        d.pos[:b].copy_(torch.from_numpy(pos).pin_memory(), non_blocking=True)
+        d.seq_lens[:b].copy_(torch.from_numpy(seq).pin_memory(), non_blocking=True)
+        d.slot[:b].copy_(torch.from_numpy(slot).pin_memory(), non_blocking=True)
+        if self.bt_dirty:
+            d.block_tables.copy_(torch.from_numpy(self.bt_host).pin_memory(), non_blocking=True)
+            self.bt_dirty = False
+        d.step(b)
+        row = len(self.hist_rows)
+        if row >= self.history.shape[0]:
+            self.flush_history()
+            row = 0
+        self.history[row, :b].copy_(d.ids[:b])
+        mapping = [None] * b
+        for s in act:
+            mapping[s.slot] = s.sid
+            s.kv_len += 1
+            s.n_generated += 1
+            s.decode_steps_served += 1
+        self.hist_rows.append(mapping)
+        self.stats["decode_tokens"] += len(act)
+        self.stats["decode_steps"] += 1
+        self.stats["peak_batch_size"] = max(self.stats["peak_batch_size"], len(act))
+        for s in act:
+            if s.done:
+                self._retire(s)
+        return len(act)
+
+    def _retire(self, s: Session):
+        s.status = "finished"
+        self._free_session(s)
+
+    # ----------------------------------------------------------------------------- outputs
+    def flush_history(self):
+        """Copy generated tokens to the host (one D2H copy) and append them to sessions."""
+        for sids, toks in self.hist_first:
+            vals = toks.cpu().tolist()
+            for sid, t in zip(sids, vals):
+                self.sessions[sid].generated.append(int(t))
+        self.hist_first = []
+        n = len(self.hist_rows)
+        if n:
+            h = self.history[:n].cpu().numpy()
+            for r, mapping in enumerate(self.hist_rows):
+                for slot_i, sid in enumerate(mapping):
+                    if sid is not None:
+                        self.sessions[sid].generated.append(int(h[r, slot_i]))
+        self.hist_rows = []
+
+    def step(self) -> None:
+        if self.waiting and self._free_slots():
+            self.prefill_step()
+        else:
+            self.decode_step()
+
+    def run(self):
+        while self.has_work():
+            self.step()
+        self.flush_history()
+
+    def generate(self, prompts: List[List[int]], max_new_tokens: int) -> List[List[int]]:
+        sids = [self.submit(p, max_new_tokens) for p in prompts]
+        self.run()
+        return [self.sessions[s].generated[:max_new_tokens] for s in sids]
+
+    def close(self):
+        self.dec.release()

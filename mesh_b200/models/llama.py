@@ -1,0 +1,189 @@
+"""Tensor-parallel Llama decoder for one rank, built from the sm_100a kernels.
+
+Per layer (reference ``forward_layer``, ``agent/src/inference/forward_pass.rs:1946-2025``):
+
+    qkv   = tcgen05 GEMM(normed, wqkv)                    (swap-AB for decode-sized T)
+    q     = RoPE(q); k,v -> paged KV pool                 (rope_kv_write)
+    attn  = paged GQA attention                           (decode: split-KV; prefill: flash)
+    part  = tcgen05 GEMM(attn, wo)                        -> own slot of the symmetric workspace
+    resid, normed = AR(part) + resid, RMSNorm(mlp_norm)   (ar_fused_norm over NVLink; TP=1: add_rmsnorm)
+    h     = tcgen05 GEMM(normed, wgu) with SiLU(gate)*up epilogue
+    part  = tcgen05 GEMM(h, wdown)
+    resid, normed = AR(part) + resid, RMSNorm(next attn_norm or final_norm)
+
+then lm_head (vocab-parallel, fp32 logits) and greedy argmax merged across ranks. The reference
+computes full-vocab logits on every rank and samples on the host (forward_pass.rs:2028-2039).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..config import EngineConfig, ModelConfig
+from .weights import DeviceWeights
+
+
+class KVPool:
+    """Paged KV pool of one rank: K and V tensors [layers, pages, kv_heads_local, page_size, D] bf16.
+    Page 0 is reserved as a scratch page for padded batch slots."""
+
+    def __init__(self, cfg: ModelConfig, local_kv_heads: int, num_pages: int, page_size: int, device):
+        shape = (cfg.num_layers, num_pages, local_kv_heads, page_size, cfg.head_dim)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.num_pages = num_pages
+        self.page_size = page_size
+
+    @staticmethod
+    def bytes_per_page(cfg: ModelConfig, local_kv_heads: int, page_size: int) -> int:
+        return 2 * cfg.num_layers * local_kv_heads * page_size * cfg.head_dim * 2
+
+
+@dataclass
+class StepMeta:
+    """Device metadata of one forward."""
+    ids: torch.Tensor            # [T] int32
+    pos: torch.Tensor            # [T] int32
+    slot: torch.Tensor           # [T] int64 page*page_size + offset (-1: no KV write)
+    block_tables: torch.Tensor   # [S, max_pages] int32
+    seq_lens: torch.Tensor       # [S] int32 keys per sequence after this step
+    cu_q: Optional[torch.Tensor] = None     # [S+1] int32 (prefill)
+    last_idx: Optional[torch.Tensor] = None  # [S] int64 rows whose logits are needed (prefill)
+    max_q_len: int = 1
+    decode: bool = True
+
+
+class LlamaRunner:
+    def __init__(self, weights: DeviceWeights, ecfg: EngineConfig, kv: KVPool, device, group=None,
+                 max_tokens: int = 8192, max_pos: int = 0):
+        self.w = weights
+        self.cfg = weights.config
+        self.ecfg = ecfg
+        self.kv = kv
+        self.device = torch.device(device)
+        self.group = group
+        self.world = weights.layout.world
+        self.rank = weights.layout.rank
+        c = self.cfg
+        self.hq = weights.layout.local_q_heads
+        self.hkv = weights.layout.local_kv_heads
+        self.D = c.head_dim
+        self.H = c.hidden_dim
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.window = ecfg.sliding_window or 0
+        self.cos, self.sin = ops.rope_tables(self.D, c.rope_base, max_pos or max(ecfg.max_seq_len, 8192) + 1,
+                                             self.device)
+        self.max_tokens = max_tokens
+        self.symm = None
+        self.use_fused_ar = self.world > 1 and ecfg.allreduce_impl != "nccl"
+        if self.use_fused_ar:
+            from ..parallel.symm import SymmWorkspace
+            self.symm = SymmWorkspace(max_tokens, self.H, self.device, group)
+        self._cand_gather = None
+
+    # ------------------------------------------------------------------------------------------
+    def _resid_normed(self, T: int):
+        if self.symm is not None:
+            return self.symm.resid(T), self.symm.normed(T)
+        return (torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device),
+                torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device))
+
+    def _two_shot(self, T: int) -> bool:
+        impl = self.ecfg.allreduce_impl
+        if impl == "oneshot":
+            return False
+        if impl == "twoshot":
+            return True
+        return T * self.H * 2 * (self.world - 1) > (1 << 20)  # > ~1 MiB read per rank: two-shot
+
+    def _reduce(self, part: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor, gamma: torch.Tensor,
+                parity: int):
+        """resid += sum_ranks(part); normed = RMSNorm(resid) * gamma."""
+        T = resid.shape[0]
+        eps = self.cfg.rms_norm_eps
+        if self.world == 1:
+            ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
+        elif self.use_fused_ar:
+            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
+        else:  # NCCL baseline
+            dist.all_reduce(part, group=self.group)
+            ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
+
+    def _part_buf(self, T: int, parity: int, scratch: dict) -> torch.Tensor:
+        if self.use_fused_ar:
+            return self.symm.partial(parity, T)
+        key = ("part", T)
+        if key not in scratch:
+            scratch[key] = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
+        return scratch[key]
+
+    # ------------------------------------------------------------------------------------------
+    def forward(self, m: StepMeta, bufs: Optional[dict] = None) -> torch.Tensor:
+        """Run all layers and the LM head; returns next-token ids [S] (int32, greedy)."""
+        c, w = self.cfg, self.w
+        bufs = {} if bufs is None else bufs
+        T = m.ids.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"step of {T} tokens exceeds runner capacity {self.max_tokens}")
+
+        def buf(name, shape, dtype=torch.bfloat16):
+            key = (name, tuple(shape), dtype)
+            t = bufs.get(key)
+            if t is None:
+                t = bufs[key] = torch.empty(shape, dtype=dtype, device=self.device)
+            return t
+
+        resid, normed = self._resid_normed(T)
+        ops.embedding(m.ids, w.embedding, resid)
+        ops.add_rmsnorm(resid, w.layers[0].attn_norm, normed, c.rms_norm_eps)
+        qkv_w = (self.hq + 2 * self.hkv) * self.D
+        qkv = buf("qkv", (T, qkv_w))
+        q = buf("q", (T, self.hq * self.D))
+        attn = buf("attn", (T, self.hq * self.D))
+        h = buf("h", (T, w.i_pad))
+        parity = 0
+        for li, L in enumerate(w.layers):
+            kc, vc = self.kv.k[li], self.kv.v[li]
+            ops.linear(normed, L.wqkv, out=qkv)
+            ops.rope_kv_write(qkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv)
+            if m.decode:
+                ops.attn_decode(q, kc, vc, m.block_tables, m.seq_lens, attn, self.scale, self.window,
+                                max_len_hint=m.max_q_len)
+            else:
+                ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
+                                 self.window)
+            part = self._part_buf(T, parity, bufs)
+            ops.linear(attn, L.wo, out=part)
+            self._reduce(part, resid, normed, L.mlp_norm, parity)
+            parity ^= 1
+            ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
+            part = self._part_buf(T, parity, bufs)
+            ops.linear(h, L.wdown, out=part)
+            gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
+            self._reduce(part, resid, normed, gamma, parity)
+            parity ^= 1
+
+        if m.last_idx is not None:
+            S = m.last_idx.shape[0]
+            final = buf("final", (S, self.H))
+            torch.index_select(normed, 0, m.last_idx, out=final)
+        else:
+            final, S = normed, T
+        logits = buf("logits", (S, w.vocab_local), torch.float32)
+        ops.linear(final, w.lm_head, out=logits, epi=ops.EPI_STORE_F32)
+        cand = buf("cand", (S, 2), torch.float32)
+        ops.argmax_partial(logits, w.vocab_start, cand)
+        ids_out = buf("next_ids", (S,), torch.int32)
+        if self.world == 1:
+            ops.argmax_merge(cand.view(1, S, 2), ids_out)
+        else:
+            gathered = buf("cand_all", (self.world, S, 2), torch.float32)
+            dist.all_gather_into_tensor(gathered.view(-1), cand.view(-1), group=self.group)
+            ops.argmax_merge(gathered, ids_out)
+        self.last_logits = logits
+        return ids_out

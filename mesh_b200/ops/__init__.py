@@ -1,0 +1,193 @@
+"""Python front-end of the sm_100a kernels in ``mesh_b200._C``.
+
+Every op here runs the hand-written CUDA kernel; there is no silent PyTorch fallback. If the
+extension is missing on a machine with a GPU, ``ext()`` raises. ``mesh_b200.ops.reference``
+holds plain fp32 PyTorch versions used only by tests as the numerical oracle.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+_EXT = None
+_LOCK = threading.Lock()
+
+# Number of kernels launched through this module (a CUDA-graph replay re-launches the kernels
+# counted while it was captured; callers multiply by replays).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1):
+    LAUNCHES[0] += n
+
+EPI_STORE_BF16 = 0
+EPI_STORE_F32 = 1
+EPI_SILU_BF16 = 2
+# decode-sized token counts use the swap-AB orientation (weights on the 128-row MMA side)
+SWAP_AB_MAX_TOKENS = 256
+
+
+def ext():
+    """Import the compiled kernel module (built in-tree by ``__graft_entry__.build()``)."""
+    global _EXT
+    if _EXT is None:
+        with _LOCK:
+            if _EXT is None:
+                try:
+                    from .. import _C  # noqa: F401
+                except ImportError as e:  # pragma: no cover - depends on the build
+                    raise RuntimeError(
+                        "mesh_b200._C is not built; run `python setup.py build_ext --inplace` "
+                        "(or __graft_entry__.build()) before using the sm_100a kernels") from e
+                _EXT = _C
+    return _EXT
+
+
+def available() -> bool:
+    try:
+        ext()
+        return torch.cuda.is_available()
+    except RuntimeError:
+        return False
+
+
+class DeviceScratch:
+    """Per-device scratch shared by the ops of one stream: error word, GEMM split-K workspace and
+    tile counters, split-KV attention scratch. Sized lazily; grows only outside graph capture."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.gemm_ws = torch.empty(0, dtype=torch.float32, device=self.device)
+        self.gemm_counters = torch.zeros(4096, dtype=torch.int32, device=self.device)
+        self.attn_ws = torch.empty(0, dtype=torch.float32, device=self.device)
+        props = torch.cuda.get_device_properties(self.device)
+        self.num_sms = props.multi_processor_count
+
+    def ensure_gemm(self, floats: int, tiles: int):
+        if self.gemm_ws.numel() < floats:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("GEMM workspace must be sized before CUDA graph capture")
+            self.gemm_ws = torch.empty(max(floats, 1 << 20), dtype=torch.float32, device=self.device)
+        if self.gemm_counters.numel() < tiles:
+            self.gemm_counters = torch.zeros(tiles * 2, dtype=torch.int32, device=self.device)
+
+    def ensure_attn(self, floats: int):
+        if self.attn_ws.numel() < floats:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("attention scratch must be sized before CUDA graph capture")
+            self.attn_ws = torch.empty(max(floats, 1 << 20), dtype=torch.float32, device=self.device)
+
+    def check(self, what: str = "kernel"):
+        v = int(self.err.item())
+        if v:
+            self.err.zero_()
+            raise RuntimeError(f"{what}: device error code {v} (1-3 pipeline wait timeout, 4 peer timeout, 5 bad argument)")
+
+
+_SCRATCH = {}
+
+
+def scratch(device=None) -> DeviceScratch:
+    dev = torch.device(device if device is not None else torch.cuda.current_device())
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    s = _SCRATCH.get(dev)
+    if s is None:
+        s = _SCRATCH[dev] = DeviceScratch(dev)
+    return s
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16, trans: bool = False,
+         bn: int = 0, splits: int = 0) -> torch.Tensor:
+    """out = a @ b.T (trans=False, out [M, N']) or out^T = a @ b.T (trans=True, out [N, M'])
+    with the tcgen05 kernel. a [M, K], b [N, K] bf16 K-contiguous."""
+    s = scratch(a.device)
+    M, N, K = a.shape[0], b.shape[0], a.shape[1]
+    plan = ext().gemm_plan(M, N, K, epi, trans, a.device.index)
+    bn_, splits_ = (bn or plan[0]), (splits or plan[1])
+    if splits_ > 1:
+        tiles = ((M + 127) // 128) * ((N + bn_ - 1) // bn_)
+        s.ensure_gemm(splits_ * tiles * 128 * bn_, tiles)
+    ext().gemm_tcgen05(a, b, out, epi, trans, bn_, splits_, s.gemm_ws, s.gemm_counters, s.err)
+    _count()
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, epi: int = EPI_STORE_BF16,
+           swap_ab: Optional[bool] = None) -> torch.Tensor:
+    """y = x @ w.T for x [T, K], w [N, K] (nn.Linear layout). Decode-sized T uses swap-AB so the
+    weight rows fill the 128-row MMA tile; large T uses the normal orientation."""
+    T, N = x.shape[0], w.shape[0]
+    n_out = N // 2 if epi == EPI_SILU_BF16 else N
+    if out is None:
+        out = torch.empty(T, n_out, device=x.device, dtype=torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16)
+    if swap_ab is None:
+        swap_ab = T <= SWAP_AB_MAX_TOKENS
+    if swap_ab:
+        return gemm(w, x, out, epi, trans=True)
+    return gemm(x, w, out, epi, trans=False)
+
+
+def add_rmsnorm(resid: torch.Tensor, gamma: torch.Tensor, normed: torch.Tensor, eps: float,
+                delta: Optional[torch.Tensor] = None):
+    ext().add_rmsnorm(delta, resid, gamma, normed, eps)
+    _count()
+    return normed
+
+
+def rope_kv_write(qkv, pos, slot, cos_t, sin_t, q_out, kcache, vcache, hq: int, hkv: int):
+    ext().rope_kv_write(qkv, pos, slot, cos_t, sin_t, q_out, kcache, vcache, hq, hkv)
+    _count()
+    return q_out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
+    ext().embedding(ids, table, out, scratch(ids.device).err)
+    _count()
+    return out
+
+
+def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, window: int = 0,
+                splits: int = 0, max_len_hint: int = 0):
+    s = scratch(q.device)
+    B, hkv, D = q.shape[0], kcache.shape[1], kcache.shape[3]
+    hq = q.shape[1] // D
+    if splits <= 0:
+        splits = ext().attn_decode_pick_splits(B, hkv, max_len_hint or block_tables.shape[1] * kcache.shape[2],
+                                               s.num_sms)
+    if splits > 1:
+        s.ensure_attn(B * hq * splits * (D + 1))
+    ext().attn_decode(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, splits, scale, window)
+    _count(2 if splits > 1 else 1)
+    return out
+
+
+def attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len: int, scale: float,
+                 window: int = 0):
+    ext().attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len, scale, window)
+    _count()
+    return out
+
+
+def argmax_partial(logits: torch.Tensor, vocab_offset: int, out: torch.Tensor):
+    ext().argmax_partial(logits, vocab_offset, out)
+    _count()
+    return out
+
+
+def argmax_merge(cand: torch.Tensor, ids: torch.Tensor):
+    ext().argmax_merge(cand, ids)
+    _count()
+    return ids
+
+
+def rope_tables(head_dim: int, base: float, max_pos: int, device) -> tuple:
+    """cos/sin [max_pos, head_dim/2] fp32; inv_freq[i] = base^(-2i/d) computed in float64."""
+    half = head_dim // 2
+    inv = 1.0 / (torch.tensor(base, dtype=torch.float64) ** (torch.arange(half, dtype=torch.float64) * 2.0 / head_dim))
+    t = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cos(t).float().to(device), torch.sin(t).float().to(device)

@@ -1,0 +1,110 @@
+"""Symmetric NVLink workspace for the fused tensor-parallel collectives.
+
+One allocation per rank, mapped into every peer of the TP group (CUDA VMM/IPC through
+``torch.distributed._symmetric_memory``). Layout (byte offsets, identical on every rank):
+
+    [flags: 2 phases x 256 blocks x 8 ranks x u32] [partial slot 0: T_max x H bf16]
+    [partial slot 1] [resid: T_max x H bf16] [normed: T_max x H bf16]
+
+The o_proj / down_proj GEMMs write their partial sums into a partial slot; the ``ar_fused_norm``
+kernel reads the peers' slots over NVLink, adds the residual, applies RMSNorm and writes
+``resid`` / ``normed`` (locally for one-shot, into every peer for two-shot). Only plain P2P loads
+and stores touch peer memory; no TMA (and no multicast TMA) ever reads a peer address.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+def _align(x: int, a: int = 256) -> int:
+    return (x + a - 1) // a * a
+
+
+@dataclass
+class SymmLayout:
+    t_max: int
+    hidden: int
+    off_flags: int
+    off_p0: int
+    off_p1: int
+    off_resid: int
+    off_normed: int
+    total: int
+
+    @classmethod
+    def make(cls, t_max: int, hidden: int, flags_bytes: int) -> "SymmLayout":
+        row = t_max * hidden * 2
+        o = 0
+        off_flags = o; o = _align(o + flags_bytes)
+        off_p0 = o; o = _align(o + row)
+        off_p1 = o; o = _align(o + row)
+        off_resid = o; o = _align(o + row)
+        off_normed = o; o = _align(o + row)
+        return cls(t_max, hidden, off_flags, off_p0, off_p1, off_resid, off_normed, o)
+
+
+class SymmWorkspace:
+    """Owns the symmetric buffer of this rank plus the peer address table."""
+
+    def __init__(self, t_max: int, hidden: int, device: torch.device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.device = device
+        self.group = group or dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.layout = SymmLayout.make(t_max, hidden, ops.ext().ar_flags_bytes())
+        self.buf = symm_mem.empty(self.layout.total, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        gname = self.group.group_name
+        try:
+            if not symm_mem.is_symm_mem_enabled_for_group(gname):
+                symm_mem.enable_symm_mem_for_group(gname)
+        except Exception:
+            pass
+        self.handle = symm_mem.rendezvous(self.buf, gname)
+        ptrs: List[int] = list(self.handle.buffer_ptrs)
+        if len(ptrs) != self.world:
+            raise RuntimeError(f"symmetric rendezvous returned {len(ptrs)} peers for world {self.world}")
+        self.bases = torch.tensor(ptrs, dtype=torch.int64)
+        self.epoch = torch.zeros(256, dtype=torch.int32, device=device)
+        dist.barrier(self.group)
+
+    def view(self, off: int, rows: int) -> torch.Tensor:
+        L = self.layout
+        n = rows * L.hidden
+        return self.buf[off: off + n * 2].view(torch.bfloat16).view(rows, L.hidden)
+
+    def partial(self, parity: int, rows: int) -> torch.Tensor:
+        return self.view(self.layout.off_p0 if parity % 2 == 0 else self.layout.off_p1, rows)
+
+    def resid(self, rows: int) -> torch.Tensor:
+        return self.view(self.layout.off_resid, rows)
+
+    def normed(self, rows: int) -> torch.Tensor:
+        return self.view(self.layout.off_normed, rows)
+
+    def fused_allreduce_norm(self, T: int, parity: int, gamma: torch.Tensor, eps: float, two_shot: bool,
+                             nblocks: int = 0, timeout_s: float = 5.0):
+        L = self.layout
+        if T > L.t_max:
+            raise ValueError(f"T={T} exceeds symmetric workspace capacity {L.t_max}")
+        if nblocks <= 0:
+            rows = (T + self.world - 1) // self.world if two_shot else T
+            nblocks = max(1, min(rows, 128))
+        s = ops.scratch(self.device)
+        ops.ext().ar_fused_norm(self.bases, L.off_flags, L.off_p0, L.off_p1, L.off_resid, L.off_normed,
+                                self.rank, self.world, T, L.hidden, parity, gamma, eps, self.epoch, s.err,
+                                nblocks, two_shot, timeout_s)
+        ops._count()
+
+    def barrier(self, timeout_s: float = 5.0):
+        s = ops.scratch(self.device)
+        ops.ext().ar_barrier(self.bases, self.layout.off_flags, self.rank, self.world, self.epoch, s.err,
+                             timeout_s, self.epoch)

@@ -1,0 +1,222 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference of the same op."""
+import math
+
+import pytest
+import torch
+
+from mesh_b200 import ops
+from mesh_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(x, y):
+    x, y = x.float(), y.float()
+    return ((x - y).norm() / (y.norm() + 1e-6)).item()
+
+
+@pytest.fixture(autouse=True)
+def _check_err():
+    yield
+    ops.scratch(torch.device("cuda", torch.cuda.current_device())).check("kernel")
+
+
+def _rand(*shape, std=1.0, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * std).to(dtype)
+
+
+# ------------------------------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 1024), (300, 200, 328), (1, 384, 4096),
+                                   (64, 6144, 4096), (17, 1000, 512), (4096, 1024, 2048)])
+@pytest.mark.parametrize("trans", [False, True])
+def test_gemm_bf16(M, N, K, trans):
+    x = _rand(M, K, seed=1)
+    w = _rand(N, K, std=0.05, seed=2)
+    want = x.float() @ w.float().T
+    if trans:  # weights on the MMA M side: out^T = w @ x^T
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        ops.gemm(w, x, out, ops.EPI_STORE_BF16, trans=True)
+    else:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        ops.gemm(x, w, out, ops.EPI_STORE_BF16, trans=False)
+    torch.cuda.synchronize()
+    assert rel_err(out, want) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5])
+@pytest.mark.parametrize("trans", [False, True])
+def test_gemm_f32_splitk(splits, trans):
+    M, N, K = 64, 768, 2048
+    x = _rand(M, K, seed=3)
+    w = _rand(N, K, std=0.05, seed=4)
+    want = x.float() @ w.float().T
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    if trans:
+        ops.gemm(w, x, out, ops.EPI_STORE_F32, trans=True, splits=splits)
+    else:
+        ops.gemm(x, w, out, ops.EPI_STORE_F32, trans=False, splits=splits)
+    torch.cuda.synchronize()
+    assert rel_err(out, want) < 2e-3
+    # counters must be left at zero so graph replays and later calls work
+    assert int(ops.scratch(torch.device(DEV, 0)).gemm_counters.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 200, 1024])
+def test_gemm_silu_mul(T):
+    K, I = 1024, 512
+    x = _rand(T, K, seed=5)
+    w = _rand(2 * I, K, std=0.05, seed=6)
+    y = x.float() @ w.float().T
+    want = ref.silu_mul_interleaved(y)
+    out = ops.linear(x, w, epi=ops.EPI_SILU_BF16)
+    torch.cuda.synchronize()
+    assert out.shape == (T, I)
+    assert rel_err(out, want) < 1e-2
+
+
+def test_linear_both_orientations_agree():
+    x = _rand(100, 512, seed=7)
+    w = _rand(640, 512, std=0.05, seed=8)
+    a = ops.linear(x, w, swap_ab=True)
+    b = ops.linear(x, w, swap_ab=False)
+    torch.cuda.synchronize()
+    assert rel_err(a, b) < 1e-2
+
+
+# ------------------------------------------------------------------------------------- norm etc.
+@pytest.mark.parametrize("H", [256, 4096, 8192])
+def test_add_rmsnorm(H):
+    T = 33
+    resid = _rand(T, H, seed=9)
+    delta = _rand(T, H, seed=10)
+    gamma = (1 + 0.1 * _rand(H, seed=11).float()).to(torch.bfloat16)
+    want_resid = (resid.float() + delta.float()).to(torch.bfloat16)
+    want = ref.rmsnorm(want_resid.float(), gamma, 1e-5)
+    normed = torch.empty_like(resid)
+    r = resid.clone()
+    ops.add_rmsnorm(r, gamma, normed, 1e-5, delta=delta)
+    torch.cuda.synchronize()
+    assert torch.equal(r, want_resid)
+    assert rel_err(normed, want) < 1e-2
+    r2 = resid.clone()
+    ops.add_rmsnorm(r2, gamma, normed, 1e-5)
+    assert rel_err(normed, ref.rmsnorm(resid.float(), gamma, 1e-5)) < 1e-2
+
+
+def test_rope_kv_write():
+    T, hq, hkv, D, ps, pages = 40, 8, 2, 128, 16, 10
+    qkv = _rand(T, (hq + 2 * hkv) * D, seed=12)
+    pos = torch.arange(100, 100 + T, dtype=torch.int32, device=DEV)
+    page_ids = torch.tensor([3, 7, 1], device=DEV)
+    p = torch.arange(T, device=DEV)
+    slot = (page_ids[p // ps] * ps + p % ps).to(torch.int64)
+    slot[5] = -1
+    cos, sin = ops.rope_tables(D, 5e5, 4096, DEV)
+    kc = torch.zeros(pages, hkv, ps, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(T, hq * D, dtype=torch.bfloat16, device=DEV)
+    ops.rope_kv_write(qkv, pos, slot, cos, sin, q, kc, vc, hq, hkv)
+    torch.cuda.synchronize()
+    qr = ref.rope(qkv[:, :hq * D], pos, D, 5e5)
+    kr = ref.rope(qkv[:, hq * D:(hq + hkv) * D], pos, D, 5e5)
+    assert rel_err(q, qr) < 1e-2
+    for t in range(T):
+        if t == 5:
+            continue
+        pg, off = int(page_ids[t // ps]), t % ps
+        assert rel_err(kc[pg, :, off].reshape(-1), kr[t]) < 1e-2
+        assert torch.equal(vc[pg, :, off].reshape(-1), qkv[t, (hq + hkv) * D:])
+    assert kc[page_ids[0], :, 5].abs().sum() == 0  # slot -1 skipped
+
+
+def test_embedding_and_argmax():
+    V, H = 1000, 256
+    table = _rand(V, H, seed=13)
+    ids = torch.tensor([0, 5, 999, 17], dtype=torch.int32, device=DEV)
+    out = torch.empty(4, H, dtype=torch.bfloat16, device=DEV)
+    ops.embedding(ids, table, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, table[ids.long()])
+    logits = torch.randn(5, 3000, device=DEV)
+    logits[2, 100] = 50.0
+    logits[2, 200] = 50.0  # tie: first index wins
+    cand = torch.empty(5, 2, device=DEV)
+    ops.argmax_partial(logits, 0, cand)
+    idx = torch.empty(5, dtype=torch.int32, device=DEV)
+    ops.argmax_merge(cand.view(1, 5, 2), idx)
+    torch.cuda.synchronize()
+    assert idx.tolist() == logits.argmax(-1).tolist()
+    assert int(idx[2]) == 100
+    # two "ranks" each holding half of the vocabulary
+    c2 = torch.empty(2, 5, 2, device=DEV)
+    ops.argmax_partial(logits[:, :1500].contiguous(), 0, c2[0])
+    ops.argmax_partial(logits[:, 1500:].contiguous(), 1500, c2[1])
+    ops.argmax_merge(c2, idx)
+    torch.cuda.synchronize()
+    assert idx.tolist() == logits.argmax(-1).tolist()
+
+
+# -------------------------------------------------------------------------------------- attention
+def _paged_kv(lens, hkv, D, ps, seed):
+    """Random K/V for sequences of the given lengths scattered over shuffled pages."""
+    npages = sum((L + ps - 1) // ps for L in lens) + 4
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(npages - 1, generator=g) + 1
+    kc = _rand(npages, hkv, ps, D, seed=seed + 1)
+    vc = _rand(npages, hkv, ps, D, seed=seed + 2)
+    maxp = max((L + ps - 1) // ps for L in lens)
+    bt = torch.zeros(len(lens), maxp, dtype=torch.int32)
+    k_list, v_list, c = [], [], 0
+    for i, L in enumerate(lens):
+        n = (L + ps - 1) // ps
+        pg = perm[c:c + n]
+        c += n
+        bt[i, :n] = pg
+        k_list.append(kc[pg.to(DEV)].permute(0, 2, 1, 3).reshape(-1, hkv, D)[:L])
+        v_list.append(vc[pg.to(DEV)].permute(0, 2, 1, 3).reshape(-1, hkv, D)[:L])
+    return kc, vc, bt.to(DEV), k_list, v_list
+
+
+@pytest.mark.parametrize("G,D", [(4, 128), (8, 128), (1, 128), (4, 64)])
+@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("window", [0, 100])
+def test_attn_decode(G, D, splits, window):
+    lens = [1, 17, 300, 1029, 64]
+    hkv, ps = 2, 16
+    hq = hkv * G
+    kc, vc, bt, ks, vs = _paged_kv(lens, hkv, D, ps, seed=20)
+    q = _rand(len(lens), hq * D, seed=30)
+    out = torch.empty_like(q)
+    scale = 1 / math.sqrt(D)
+    ops.attn_decode(q, kc, vc, bt, torch.tensor(lens, dtype=torch.int32, device=DEV), out, scale, window, splits=splits)
+    torch.cuda.synchronize()
+    for i, L in enumerate(lens):
+        want = ref.attention(q[i].view(1, hq, D), ks[i], vs[i], torch.tensor([L - 1], device=DEV),
+                             torch.arange(L, device=DEV), scale, window)
+        assert rel_err(out[i].view(1, hq, D), want) < 2e-2, (i, L)
+
+
+@pytest.mark.parametrize("G", [4, 8, 1])
+@pytest.mark.parametrize("window", [0, 50])
+def test_attn_prefill_varlen_prefix(G, window):
+    hkv, D, ps = 2, 128, 16
+    hq = hkv * G
+    k_lens = [40, 300, 129, 64]
+    q_lens = [40, 100, 1, 64]   # seq 1 and 2 have cached prefixes
+    kc, vc, bt, ks, vs = _paged_kv(k_lens, hkv, D, ps, seed=40)
+    T = sum(q_lens)
+    q = _rand(T, hq * D, seed=41)
+    out = torch.empty_like(q)
+    cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(D)
+    ops.attn_prefill(q, kc, vc, cu, torch.tensor(k_lens, dtype=torch.int32, device=DEV), bt, out, max(q_lens), scale,
+                     window)
+    torch.cuda.synchronize()
+    for i, (kl, ql) in enumerate(zip(k_lens, q_lens)):
+        a = int(cu[i])
+        qpos = torch.arange(kl - ql, kl, device=DEV)
+        want = ref.attention(q[a:a + ql].view(ql, hq, D), ks[i], vs[i], qpos, torch.arange(kl, device=DEV), scale,
+                             window)
+        assert rel_err(out[a:a + ql].view(ql, hq, D), want) < 2e-2, i
