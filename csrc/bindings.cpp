@@ -3,7 +3,8 @@
 
 namespace mesh {
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn,
-                  int64_t splits, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err);
+                  int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                  const c10::optional<at::Tensor>& trace);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device);
 void add_rmsnorm(const c10::optional<at::Tensor>& delta, at::Tensor& resid, const at::Tensor& gamma, at::Tensor& normed,
                  double eps);
@@ -13,10 +14,14 @@ void rope_kv_write(const at::Tensor& qkv, const at::Tensor& pos, const at::Tenso
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void argmax_partial(const at::Tensor& logits, int64_t vocab_offset, at::Tensor& out);
 void argmax_merge(const at::Tensor& cand, at::Tensor& ids);
+void argmax_tiles(const at::Tensor& cand, int64_t vocab_offset, at::Tensor& out);
 void attn_decode(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
                  const at::Tensor& block_tables, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& ws,
                  int64_t splits, double scale, int64_t window);
 int64_t attn_decode_pick_splits(int64_t B, int64_t hkv, int64_t max_len, int64_t num_sms);
+void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
+                    const at::Tensor& block_tables, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& ws,
+                    at::Tensor& err, int64_t splits, double scale, int64_t window);
 void attn_prefill(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache, const at::Tensor& cu_q,
                   const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
                   double scale, int64_t window);
@@ -31,14 +36,18 @@ int64_t ar_flags_bytes();
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mesh_b200 sm_100a kernels";
-  m.def("gemm_tcgen05", &mesh::gemm_tcgen05, "tcgen05 GEMM out = A @ B^T (or its transpose)");
-  m.def("gemm_plan", &mesh::gemm_plan, "tile plan [bn, splits, workspace_floats, tiles, stages]");
+  m.def("gemm_tcgen05", &mesh::gemm_tcgen05, "tcgen05 GEMM out = A @ B^T (or its transpose)", py::arg("A"),
+        py::arg("B"), py::arg("out"), py::arg("epi"), py::arg("trans"), py::arg("bn"), py::arg("mode"),
+        py::arg("workspace"), py::arg("counters"), py::arg("err"), py::arg("trace") = py::none());
+  m.def("gemm_plan", &mesh::gemm_plan, "tile plan [bn, workspace_floats, stream-K tiles, stages, grid, dp_tiles, sk_iters]");
   m.def("add_rmsnorm", &mesh::add_rmsnorm, "resid += delta; normed = rmsnorm(resid) * gamma");
   m.def("rope_kv_write", &mesh::rope_kv_write, "RoPE on q/k + paged KV write");
   m.def("embedding", &mesh::embedding, "embedding gather");
   m.def("argmax_partial", &mesh::argmax_partial, "per-row (max, global index) over local vocab");
   m.def("argmax_merge", &mesh::argmax_merge, "merge per-rank argmax candidates");
+  m.def("argmax_tiles", &mesh::argmax_tiles, "reduce LM-head per-tile argmax candidates");
   m.def("attn_decode", &mesh::attn_decode, "paged GQA decode attention (split-KV)");
+  m.def("attn_decode_tc", &mesh::attn_decode_tc, "paged GQA decode attention, TMA-streamed tensor-core variant");
   m.def("attn_decode_pick_splits", &mesh::attn_decode_pick_splits, "split-KV heuristic");
   m.def("attn_prefill", &mesh::attn_prefill, "paged causal varlen GQA prefill attention");
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");

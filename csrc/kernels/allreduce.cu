@@ -22,6 +22,7 @@
 #include <torch/extension.h>
 
 #include "../include/sm100.cuh"
+#include "../include/launch.h"
 
 namespace mesh {
 
@@ -143,6 +144,8 @@ __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   __shared__ int s_ok;
   __shared__ uint32_t s_epoch;
   const int b = blockIdx.x;
+  griddep_wait();  // partials come from the GEMM just before
+  griddep_launch_dependents();
   if (threadIdx.x == 0) s_epoch = a.epoch[b] + 1;
   __syncthreads();
   const uint32_t e = s_epoch;
@@ -204,9 +207,9 @@ void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, i
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = (int)nblocks;
   if (two_shot)
-    ar_norm_kernel<4, true><<<nb, AR_THREADS, 0, st>>>(a);
+    launch_k(ar_norm_kernel<4, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
   else
-    ar_norm_kernel<4, false><<<nb, AR_THREADS, 0, st>>>(a);
+    launch_k(ar_norm_kernel<4, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -214,6 +217,7 @@ void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, i
 __global__ void ar_barrier_kernel(const ArArgs a) {
   __shared__ int s_ok;
   __shared__ uint32_t s_epoch;
+  griddep_wait();
   if (threadIdx.x == 0) s_epoch = a.epoch[AR_MAX_BLOCKS - 1] + 1;
   __syncthreads();
   block_barrier(a, 0, s_epoch, &s_ok);

@@ -19,6 +19,8 @@
 
 #include "../include/sm100.cuh"
 #include "attn_decode.cuh"
+#include "attn_decode_tc.cuh"
+#include "../include/tma_host.h"
 
 namespace mesh {
 
@@ -57,6 +59,48 @@ void attn_decode(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.window = (int)window;
   launch_attn_decode(a, B, G, D, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// TMA-streamed tensor-core variant (head_dim 128, 16-token pages).
+void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
+                    const at::Tensor& block_tables, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& ws,
+                    at::Tensor& err, int64_t splits, double scale, int64_t window) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous(), "attn_decode_tc: q bf16 [B, hq*D]");
+  TORCH_CHECK(kcache.dim() == 4 && kcache.sizes() == vcache.sizes() && kcache.is_contiguous() && vcache.is_contiguous(),
+              "attn_decode_tc: cache [pages, hkv, 16, 128] contiguous");
+  TORCH_CHECK(kcache.size(2) == 16 && kcache.size(3) == 128, "attn_decode_tc: page 16, head_dim 128");
+  const int B = q.size(0), hkv = kcache.size(1);
+  const int hq = q.size(1) / 128;
+  const int G = hq / hkv;
+  TORCH_CHECK(hq % hkv == 0 && (G == 1 || G == 2 || G == 4 || G == 8), "attn_decode_tc: group size 1/2/4/8");
+  if (B == 0) return;
+  if (splits < 1) splits = 1;
+  if (splits > 1)
+    TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= (int64_t)B * hq * splits * 129, "attn_decode_tc: scratch");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const uint64_t rows = (uint64_t)kcache.size(0) * hkv * 16;
+  CUtensorMap tk = tma_map_2d_bf16(kcache.data_ptr(), 128, rows, 128, 64, 16);
+  CUtensorMap tv = tma_map_2d_bf16(vcache.data_ptr(), 128, rows, 128, 64, 16);
+  DecodeTcArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ws = splits > 1 ? ws.data_ptr<float>() : nullptr;
+  a.err = err.data_ptr<int>();
+  a.max_pages = block_tables.size(1);
+  a.hkv = hkv;
+  a.splits = (int)splits;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.window = (int)window;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (G) {
+    case 1: launch_attn_decode_tc_g<1>(tk, tv, a, B, st); break;
+    case 2: launch_attn_decode_tc_g<2>(tk, tv, a, B, st); break;
+    case 4: launch_attn_decode_tc_g<4>(tk, tv, a, B, st); break;
+    default: launch_attn_decode_tc_g<8>(tk, tv, a, B, st); break;
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "../include/sm100.cuh"
+#include "../include/launch.h"
 
 namespace mesh {
 
@@ -25,6 +26,8 @@ constexpr int DEC_WARPS = 4;
 
 template <int G, int D>
 __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const DecodeArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int DPL = D / 32;  // head dims per lane in P.V
   __shared__ float q_s[G][D];
   __shared__ float red_m[DEC_WARPS][G];
@@ -63,20 +66,21 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const Decod
   for (int blk = t_begin + warp * 32; blk < t_end; blk += DEC_WARPS * 32) {
     const int t = blk + lane;
     const bool valid = t < t_end;
+    const int ts = valid ? t : blk;  // lanes past the end reuse a valid key address, weight 0
+    const int pg_i = ts / a.page_size;
+    const int page = bt[pg_i];
+    const long base = (long)page * page_stride + h * head_stride + (long)(ts - pg_i * a.page_size) * D;
     float s[G];
-    long vbase = 0;
-    if (valid) {
-      const int page = bt[t / a.page_size];
-      const int off = t - (t / a.page_size) * a.page_size;
-      const long base = (long)page * page_stride + h * head_stride + (long)off * D;
-      vbase = base;
-      const uint4* kr = reinterpret_cast<const uint4*>(a.k + base);
 #pragma unroll
-      for (int g = 0; g < G; ++g) s[g] = 0.f;
-#pragma unroll 4
+    for (int g = 0; g < G; ++g) s[g] = 0.f;
+    {
+      const uint4* kr = reinterpret_cast<const uint4*>(a.k + base);
+      uint4 kv[D / 8];
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) kv[c] = __ldg(kr + c);
+#pragma unroll
       for (int c = 0; c < D / 8; ++c) {
-        uint4 kv = kr[c];
-        const uint32_t* ku = reinterpret_cast<const uint32_t*>(&kv);
+        const uint32_t* ku = reinterpret_cast<const uint32_t*>(&kv[c]);
         float kf[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) unpack_bf16x2(ku[j], kf[2 * j], kf[2 * j + 1]);
@@ -86,35 +90,34 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const Decod
           for (int j = 0; j < 8; ++j) s[g] += q_s[g][c * 8 + j] * kf[j];
         }
       }
-    } else {
-#pragma unroll
-      for (int g = 0; g < G; ++g) s[g] = -INFINITY;
     }
     float p[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float mx = s[g];
+      float sv = valid ? s[g] : -INFINITY;
+      float mx = sv;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float mn = fmaxf(m[g], mx);
       const float corr = exp2f(m[g] - mn);  // m = -inf initially -> 0
-      p[g] = valid ? exp2f(s[g] - mn) : 0.f;
+      p[g] = valid ? exp2f(sv - mn) : 0.f;
       l[g] = l[g] * corr + p[g];
 #pragma unroll
       for (int i = 0; i < DPL; ++i) acc[g][i] *= corr;
       m[g] = mn;
     }
-    const int cnt = min(32, t_end - blk);
-    for (int j = 0; j < cnt; ++j) {
-      const long vb = __shfl_sync(0xffffffffu, vbase, j);
+    // P.V: lane owns DPL dims; 32 key rows, 8 loads in flight
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+      const long vb = __shfl_sync(0xffffffffu, base, j);
       const __nv_bfloat16* vr = a.v + vb + lane * DPL;
       float vf[DPL];
       if constexpr (DPL == 4) {
-        uint2 vv = *reinterpret_cast<const uint2*>(vr);
+        uint2 vv = __ldg(reinterpret_cast<const uint2*>(vr));
         unpack_bf16x2(vv.x, vf[0], vf[1]);
         unpack_bf16x2(vv.y, vf[2], vf[3]);
       } else {
-        uint32_t vv = *reinterpret_cast<const uint32_t*>(vr);
+        uint32_t vv = __ldg(reinterpret_cast<const unsigned int*>(vr));
         unpack_bf16x2(vv, vf[0], vf[1]);
       }
 #pragma unroll
@@ -169,6 +172,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const Decod
 template <int D>
 __global__ void attn_decode_combine_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int hq,
                                            int splits) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int seq = blockIdx.x, qh = blockIdx.y;
   const float* w = ws + ((long)seq * hq + qh) * splits * (D + 1);
   float M = -INFINITY;
@@ -189,8 +194,10 @@ __global__ void attn_decode_combine_kernel(const float* __restrict__ ws, __nv_bf
 template <int G, int D>
 inline void launch_attn_decode_gd(const DecodeArgs& a, int B, cudaStream_t st) {
   dim3 grid(B, a.hkv, a.splits);
-  attn_decode_kernel<G, D><<<grid, DEC_WARPS * 32, 0, st>>>(a);
-  if (a.splits > 1) attn_decode_combine_kernel<D><<<dim3(B, a.hkv * G), D, 0, st>>>(a.ws, a.out, a.hkv * G, a.splits);
+  launch_k(attn_decode_kernel<G, D>, grid, dim3(DEC_WARPS * 32), 0, st, a);
+  if (a.splits > 1)
+    launch_k(attn_decode_combine_kernel<D>, dim3(B, a.hkv * G), dim3(D), 0, st, (const float*)a.ws, a.out,
+             a.hkv * G, a.splits);
 }
 
 template <int D>

@@ -16,6 +16,7 @@
 #include <torch/extension.h>
 
 #include "../include/sm100.cuh"
+#include "../include/launch.h"
 
 namespace mesh {
 
@@ -72,6 +73,8 @@ template <int G>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const PrefillArgs a) {
   constexpr int BQ = PF_ROWS / G;
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_wait();
+  griddep_launch_dependents();
   uint8_t* q_sm = smem;
   uint8_t* k_sm = smem + PF_ROWS * PF_D * 2;              // 2 buffers
   uint8_t* v_sm = k_sm + 2 * PF_KEYS * PF_D * 2;          // 2 buffers
@@ -298,7 +301,7 @@ void attn_prefill(const at::Tensor& q, const at::Tensor& kcache, const at::Tenso
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto go = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 128, smem, st>>>(a);
+    launch_k(kern, grid, dim3(128), smem, st, a);
   };
   switch (G) {
     case 1: go(attn_prefill_kernel<1>); break;

@@ -13,6 +13,7 @@
 #include <torch/extension.h>
 
 #include "../include/sm100.cuh"
+#include "../include/launch.h"
 
 namespace mesh {
 
@@ -42,6 +43,8 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ resid,
                                                          const __nv_bfloat16* __restrict__ gamma,
                                                          __nv_bfloat16* __restrict__ normed, int H, float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int nvec = H / 8;
@@ -117,9 +120,9 @@ void add_rmsnorm(const c10::optional<at::Tensor>& delta, at::Tensor& resid, cons
     TORCH_CHECK(delta->sizes() == resid.sizes() && delta->is_contiguous(), "add_rmsnorm: delta");
     d = reinterpret_cast<const __nv_bfloat16*>(delta->data_ptr());
   }
-  add_rmsnorm_kernel<256><<<rows, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      d, reinterpret_cast<__nv_bfloat16*>(resid.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(normed.data_ptr()), H, (float)eps);
+  launch_k(add_rmsnorm_kernel<256>, dim3(rows), dim3(256), 0, at::cuda::getCurrentCUDAStream(), d,
+           reinterpret_cast<__nv_bfloat16*>(resid.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()),
+           reinterpret_cast<__nv_bfloat16*>(normed.data_ptr()), H, (float)eps);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -133,6 +136,8 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, cons
                                      const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ q_out,
                                      __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache, int hq,
                                      int hkv, int D, int page_size) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long t = blockIdx.x;
   const int width = (hq + 2 * hkv) * D;
   const __nv_bfloat16* row = qkv + t * width;
@@ -198,11 +203,12 @@ void rope_kv_write(const at::Tensor& qkv, const at::Tensor& pos, const at::Tenso
   const long T = qkv.size(0);
   if (T == 0) return;
   const c10::cuda::CUDAGuard guard(qkv.device());
-  rope_kv_write_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), pos.data_ptr<int>(), reinterpret_cast<const long*>(slot.data_ptr<int64_t>()),
-      cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(kcache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr()),
-      (int)hq, (int)hkv, D, ps);
+  launch_k(rope_kv_write_kernel, dim3(T), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (const int*)pos.data_ptr<int>(),
+           reinterpret_cast<const long*>(slot.data_ptr<int64_t>()), (const float*)cos_t.data_ptr<float>(),
+           (const float*)sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+           reinterpret_cast<__nv_bfloat16*>(kcache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr()),
+           (int)hq, (int)hkv, D, ps);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -212,6 +218,8 @@ void rope_kv_write(const at::Tensor& qkv, const at::Tensor& pos, const at::Tenso
 // ----------------------------------------------------------------------------------------------
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int V, int H, int* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long t = blockIdx.x;
   const int id = ids[t];
   const int nvec = H / 8;
@@ -232,9 +240,9 @@ void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, 
   const long T = ids.numel();
   if (T == 0) return;
   const c10::cuda::CUDAGuard guard(ids.device());
-  embed_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)table.size(0), H, err.data_ptr<int>());
+  launch_k(embed_kernel, dim3(T), dim3(128), 0, at::cuda::getCurrentCUDAStream(), (const int*)ids.data_ptr<int>(),
+           reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+           (int)table.size(0), H, err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -244,6 +252,8 @@ void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, 
 // ----------------------------------------------------------------------------------------------
 __global__ void argmax_kernel(const float* __restrict__ logits, int Vloc, long ld, int vocab_offset,
                               float2* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float sv[32];
   __shared__ int si[32];
   const long b = blockIdx.x;
@@ -292,6 +302,8 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int Vloc, long l
 // Merge per-rank (value, index) candidates [R, B] into token ids [B] (int32): max value, lowest
 // index among ties, which equals the first-index argmax over the concatenated vocabulary.
 __global__ void argmax_merge_kernel(const float2* __restrict__ cand, int R, int B, int* __restrict__ ids) {
+  griddep_wait();
+  griddep_launch_dependents();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   float best = -INFINITY;
@@ -307,14 +319,76 @@ __global__ void argmax_merge_kernel(const float2* __restrict__ cand, int R, int 
   ids[b] = bi;
 }
 
+// Reduce the LM-head GEMM's per-tile candidates [m_tiles, B] (value, local index) to one
+// (value, global index) per token. One CTA per token.
+__global__ void argmax_tiles_kernel(const float2* __restrict__ cand, int m_tiles, int B, int vocab_offset,
+                                    float2* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int b = blockIdx.x;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < m_tiles; t += blockDim.x) {
+    const float2 c = cand[(long)t * B + b];
+    const int ci = __float_as_int(c.y);
+    if (c.x > best || (c.x == best && ci < bi)) {
+      best = c.x;
+      bi = ci;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = l < nw ? sv[l] : -INFINITY;
+    bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) out[b] = make_float2(best, __int_as_float(bi + vocab_offset));
+  }
+}
+
+void argmax_tiles(const at::Tensor& cand, int64_t vocab_offset, at::Tensor& out) {
+  TORCH_CHECK(cand.scalar_type() == at::kFloat && cand.dim() == 3 && cand.size(2) == 2, "argmax_tiles: [T,B,2]");
+  const int m_tiles = cand.size(0), B = cand.size(1);
+  if (B == 0) return;
+  const c10::cuda::CUDAGuard guard(cand.device());
+  launch_k(argmax_tiles_kernel, dim3(B), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const float2*>(cand.data_ptr<float>()), m_tiles, B, (int)vocab_offset,
+           reinterpret_cast<float2*>(out.data_ptr<float>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void argmax_partial(const at::Tensor& logits, int64_t vocab_offset, at::Tensor& out) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "argmax_partial: fp32 logits");
   const long B = logits.size(0);
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(logits.device());
-  argmax_kernel<<<B, 512, 0, at::cuda::getCurrentCUDAStream()>>>(logits.data_ptr<float>(), (int)logits.size(1),
-                                                                  logits.stride(0), (int)vocab_offset,
-                                                                  reinterpret_cast<float2*>(out.data_ptr<float>()));
+  launch_k(argmax_kernel, dim3(B), dim3(512), 0, at::cuda::getCurrentCUDAStream(),
+           (const float*)logits.data_ptr<float>(), (int)logits.size(1), (long)logits.stride(0), (int)vocab_offset,
+           reinterpret_cast<float2*>(out.data_ptr<float>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -323,8 +397,8 @@ void argmax_merge(const at::Tensor& cand, at::Tensor& ids) {
   const int R = cand.size(0), B = cand.size(1);
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(cand.device());
-  argmax_merge_kernel<<<(B + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const float2*>(cand.data_ptr<float>()), R, B, ids.data_ptr<int>());
+  launch_k(argmax_merge_kernel, dim3((B + 127) / 128), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+           reinterpret_cast<const float2*>(cand.data_ptr<float>()), R, B, ids.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -10,8 +10,10 @@
 //  * normal (TRANS=false): out[m][n]; used for prefill (A = activations, B = weights);
 //  * swap-AB (TRANS=true): out[n][m]; used for decode (A = weights so the 128-row MMA M dimension
 //    runs over output features and the few decode tokens form a narrow N = BN tile).
-// Small grids use split-K: every split writes an fp32 partial tile to a workspace, and the last
-// CTA to arrive on the tile's counter (atomic ticket, no spinning) sums them and runs the epilogue.
+// Scheduling: whole tiles round-robin over a persistent grid, plus stream-K for the tail waves
+// (and for decode shapes with fewer tiles than SMs): k-iterations are split evenly over the CTAs;
+// contributors to a tile publish fp32 partials and the tile's owner CTA (the one holding its
+// first k-block) adds them to its own TMEM accumulator in a fixed order.
 //
 // Epilogues: bf16 store, f32 store, and SiLU(gate)*up for gate/up weights interleaved in blocks
 // of 64 features (rows g0..63,u0..63,g64..127,...), which writes half as many features.
@@ -27,10 +29,11 @@
 
 #include "../include/sm100.cuh"
 #include "../include/tma_host.h"
+#include "../include/launch.h"
 
 namespace mesh {
 
-enum EpiKind : int { EPI_STORE_BF16 = 0, EPI_STORE_F32 = 1, EPI_SILU_BF16 = 2 };
+enum EpiKind : int { EPI_STORE_BF16 = 0, EPI_STORE_F32 = 1, EPI_SILU_BF16 = 2, EPI_ARGMAX = 3 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -42,15 +45,18 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: far above any legal w
 
 struct GemmParams {
   int M, N, K;
-  int m_tiles, n_tiles, k_blocks, splits;
+  int m_tiles, n_tiles, k_blocks;
+  int dp_tiles;       // tiles [0, dp_tiles) are owned whole, round-robin over the grid
+  int sk_iters_per_cta;  // stream-K share of the remaining tiles' k-iterations (0: none)
   int bn, stages;
   void* out;
   long ldo;
-  float* workspace;   // [splits][tiles][BM][bn]
-  int* counters;      // [tiles], zero on entry, left zero on exit
+  float* workspace;   // stream-K partial tiles: slot (sk_tile + cta) x [BM][bn] fp32
+  int* counters;      // [stream-K tiles], zero on entry, left zero on exit
   int* err;
   uint32_t idesc;
   uint32_t tmem_cols;
+  unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (nullptr: off)
 };
 
 struct Smem {
@@ -61,6 +67,7 @@ struct Smem {
   uint64_t* empty;
   uint64_t* tfull;
   uint64_t* tempty;
+  uint64_t* fixbar;   // stream-K owner: partial tiles landed
   uint32_t* tmem_base;
   int* abort_flag;
   int* epi_flag;
@@ -82,7 +89,8 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
   s.empty = s.full + p.stages;
   s.tfull = s.empty + p.stages;
   s.tempty = s.tfull + 2;
-  s.tmem_base = reinterpret_cast<uint32_t*>(s.tempty + 2);
+  s.fixbar = s.tempty + 2;
+  s.tmem_base = reinterpret_cast<uint32_t*>(s.fixbar + 1);
   s.abort_flag = reinterpret_cast<int*>(s.tmem_base + 1);
   s.epi_flag = s.abort_flag + 1;
   return s;
@@ -90,40 +98,87 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
 
 __host__ __device__ inline size_t gemm_smem_bytes(int stages, int bn) {
   return 1024 + (size_t)stages * (A_STAGE_BYTES + bn * BK * 2) + 2 * EPI_SLOT_FLOATS * sizeof(float) + 8 +
-         (size_t)(2 * stages + 4) * 8 + 16;
+         (size_t)(2 * stages + 5) * 8 + 16;
 }
 
-struct Unit {
-  int tm, tn, split, tile, kb0, kb1;
+// A segment is a contiguous k-range of one output tile processed by one CTA. Data-parallel
+// tiles are single segments; stream-K tiles are split across the CTAs whose k-iteration ranges
+// cover them ("contributors", fixed by the static partition, so results are deterministic).
+struct Seg {
+  int tile, tm, tn, kb0, kb1;
+  int sk_tile;     // -1 for whole tiles
+  int contrib, ncontrib, first_cta;
 };
 
-__device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p) {
-  const int tiles = p.m_tiles * p.n_tiles;
-  Unit r;
-  r.split = u / tiles;
-  int t = u - r.split * tiles;
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
   // grouped raster: 8 consecutive m-tiles sweep all n-tiles before the next group
   const int G = 8;
   const int group_size = G * p.n_tiles;
-  int g = t / group_size;
-  int first_m = g * G;
-  int gm = min(p.m_tiles - first_m, G);
-  int in = t - g * group_size;
-  r.tm = first_m + in % gm;
-  r.tn = in / gm;
-  r.tile = r.tm * p.n_tiles + r.tn;
-  r.kb0 = (int)(((long)r.split * p.k_blocks) / p.splits);
-  r.kb1 = (int)(((long)(r.split + 1) * p.k_blocks) / p.splits);
-  return r;
+  const int g = t / group_size;
+  const int first_m = g * G;
+  const int gm = min(p.m_tiles - first_m, G);
+  const int in = t - g * group_size;
+  tm = first_m + in % gm;
+  tn = in / gm;
 }
+
+struct SegIter {
+  int i;          // next data-parallel tile ordinal of this CTA
+  long g;         // next stream-K global iteration
+  long g_end;
+  __device__ void init(const GemmParams& p) {
+    i = 0;
+    g = (long)blockIdx.x * p.sk_iters_per_cta;
+    const long sk_total = (long)(p.m_tiles * p.n_tiles - p.dp_tiles) * p.k_blocks;
+    g_end = min(g + (long)p.sk_iters_per_cta, sk_total);
+    if (p.sk_iters_per_cta == 0) g_end = g;
+  }
+  __device__ bool next(const GemmParams& p, Seg& s) {
+    const int t_dp = blockIdx.x + i * gridDim.x;
+    if (t_dp < p.dp_tiles) {
+      ++i;
+      s.tile = t_dp;
+      tile_coords(t_dp, p, s.tm, s.tn);
+      s.kb0 = 0;
+      s.kb1 = p.k_blocks;
+      s.sk_tile = -1;
+      s.contrib = 0;
+      s.ncontrib = 1;
+      s.first_cta = 0;
+      return true;
+    }
+    if (g >= g_end) return false;
+    const int kb = p.k_blocks;
+    const long W = p.sk_iters_per_cta;
+    const int st = (int)(g / kb);
+    const int k0 = (int)(g - (long)st * kb);
+    const long tile_end = (long)(st + 1) * kb;
+    const long seg_end = min(tile_end, g_end);
+    s.sk_tile = st;
+    s.tile = p.dp_tiles + st;
+    tile_coords(s.tile, p, s.tm, s.tn);
+    s.kb0 = k0;
+    s.kb1 = k0 + (int)(seg_end - g);
+    const int first = (int)(((long)st * kb) / W);
+    const int last = (int)((tile_end - 1) / W);
+    s.first_cta = first;
+    s.contrib = blockIdx.x - first;
+    s.ncontrib = last - first + 1;
+    g = seg_end;
+    return true;
+  }
+};
 
 // ----------------------------------------------------------------------------------------------
 // epilogue helpers: the epilogue stages 128 x (<=32) fp32 chunks in smem, then writes them with a
 // thread mapping chosen for coalescing in each orientation.
 // ----------------------------------------------------------------------------------------------
 template <int EPI, bool TRANS>
-__device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float* slot0, const float* slot1,
+__device__ __forceinline__ void finalize_chunk(const GemmParams& p, uint32_t slot0, uint32_t slot1,
                                                int tm, int tn, int c0, int cw, int et) {
+  // slot0/slot1: shared-window addresses of the staged fp32 chunks ([BM][EPI_LD])
+  auto S0 = [&](int r, int c) { return lds_f32(slot0 + (uint32_t)(r * EPI_LD + c) * 4); };
+  auto S1 = [&](int r, int c) { return lds_f32(slot1 + (uint32_t)(r * EPI_LD + c) * 4); };
   const int m_base = tm * BM;
   if constexpr (EPI == EPI_SILU_BF16) {
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
@@ -136,8 +191,8 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int n = tn * p.bn + c0 + c;
         int r = rp * 2;
         if (n >= p.N || m_out_base + r >= m_out_lim) continue;
-        float g0 = slot0[r * EPI_LD + c], g1 = slot0[(r + 1) * EPI_LD + c];
-        float u0 = slot0[(r + 64) * EPI_LD + c], u1 = slot0[(r + 65) * EPI_LD + c];
+        float g0 = S0(r, c), g1 = S0((r + 1), c);
+        float u0 = S0((r + 64), c), u1 = S0((r + 65), c);
         uint32_t v = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
         *reinterpret_cast<uint32_t*>(out + (long)n * p.ldo + m_out_base + r) = v;
       }
@@ -150,8 +205,8 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int m = m_base + r;
         int n = n_out_base + cp;
         if (m >= p.M || n >= n_out_lim) continue;
-        float g0 = slot0[r * EPI_LD + cp], g1 = slot0[r * EPI_LD + cp + 1];
-        float u0 = slot1[r * EPI_LD + cp], u1 = slot1[r * EPI_LD + cp + 1];
+        float g0 = S0(r, cp), g1 = S0(r, cp + 1);
+        float u0 = S1(r, cp), u1 = S1(r, cp + 1);
         *reinterpret_cast<uint32_t*>(out + (long)m * p.ldo + n) = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
       }
     }
@@ -163,8 +218,8 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int n = tn * p.bn + c0 + c;
         int m = m_base + rp * 2;
         if (n >= p.N || m >= p.M) continue;
-        float a = slot0[(rp * 2) * EPI_LD + c];
-        float b = (m + 1 < p.M) ? slot0[(rp * 2 + 1) * EPI_LD + c] : 0.f;
+        float a = S0((rp * 2), c);
+        float b = (m + 1 < p.M) ? S0((rp * 2 + 1), c) : 0.f;
         if (m + 1 < p.M)
           *reinterpret_cast<uint32_t*>(out + (long)n * p.ldo + m) = pack_bf16x2(a, b);
         else
@@ -177,12 +232,43 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int m = m_base + r;
         int n = tn * p.bn + c0 + cp;
         if (m >= p.M || n >= p.N) continue;
-        float a = slot0[r * EPI_LD + cp], b = slot0[r * EPI_LD + cp + 1];
+        float a = S0(r, cp), b = S0(r, cp + 1);
         if (n + 1 < p.N)
           *reinterpret_cast<uint32_t*>(out + (long)m * p.ldo + n) = pack_bf16x2(a, b);
         else
           out[(long)m * p.ldo + n] = f2bf(a);
       }
+    }
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    // swap-AB LM head: rows are vocabulary entries, columns tokens. Per token keep the max over
+    // this tile's 128 rows (first index on ties); out is float2 [m_tiles][ldo] (value, index bits).
+    static_assert(TRANS, "argmax epilogue runs in swap-AB orientation");
+    const int c = et >> 2, q = et & 3;
+    if (c < cw) {
+      const int n = tn * p.bn + c0 + c;
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int r = q * 32; r < q * 32 + 32; ++r) {
+        const int m = m_base + r;
+        if (m < p.M) {
+          const float v = S0(r, c);
+          if (v > best) {
+            best = v;
+            bi = m;
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+          best = ov;
+          bi = oi;
+        }
+      }
+      if (q == 0 && n < p.N)
+        reinterpret_cast<float2*>(p.out)[(long)tm * p.ldo + n] = make_float2(best, __int_as_float(bi));
     }
   } else {  // EPI_STORE_F32
     float* out = reinterpret_cast<float*>(p.out);
@@ -192,7 +278,7 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int n = tn * p.bn + c0 + c;
         int m = m_base + r;
         if (n >= p.N || m >= p.M) continue;
-        out[(long)n * p.ldo + m] = slot0[r * EPI_LD + c];
+        out[(long)n * p.ldo + m] = S0(r, c);
       }
     } else {
       for (int idx = et; idx < BM * cw; idx += 128) {
@@ -200,7 +286,7 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, const float*
         int m = m_base + r;
         int n = tn * p.bn + c0 + c;
         if (m >= p.M || n >= p.N) continue;
-        out[(long)m * p.ldo + n] = slot0[r * EPI_LD + c];
+        out[(long)m * p.ldo + n] = S0(r, c);
       }
     }
   }
@@ -231,17 +317,18 @@ struct ChunkPlan {
   }
 };
 
-__device__ __forceinline__ void tmem_chunk_to_smem(uint32_t taddr_row, int col, int cw, float* slot, int row) {
+__device__ __forceinline__ void tmem_chunk_to_smem(uint32_t taddr_row, int col, int cw, uint32_t slot, int row) {
   uint32_t r[16];
+  const uint32_t base = slot + (uint32_t)(row * EPI_LD) * 4;
   tmem_ld16(taddr_row + col, r);
   tmem_ld_wait();
 #pragma unroll
-  for (int i = 0; i < 16; ++i) slot[row * EPI_LD + i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) sts_f32(base + i * 4, __uint_as_float(r[i]));
   if (cw > 16) {
     tmem_ld16(taddr_row + col + 16, r);
     tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) slot[row * EPI_LD + 16 + i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) sts_f32(base + (16 + i) * 4, __uint_as_float(r[i]));
   }
 }
 
@@ -253,8 +340,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   Smem s = carve(smem_raw, p);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int total_units = tiles * p.splits;
   const uint32_t b_stage_bytes = (uint32_t)p.bn * BK * 2;
 
   if (threadIdx.x == 0) {
@@ -266,6 +351,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], 128);
     }
+    mbar_init(s.fixbar, 1);
     *s.abort_flag = 0;
     fence_mbar_init();
   }
@@ -282,6 +368,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_base;
   volatile int* abort_flag = s.abort_flag;
+  unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * 16 : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = globaltimer_ns();
+  // the next kernel may start its prologue on SMs this grid frees up
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------
@@ -292,23 +382,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        Unit un = decode_unit(u, p);
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+      SegIter itr;
+      itr.init(p);
+      Seg sg;
+      bool first_seg = true;
+      while (ok && itr.next(p, sg)) {
+        int kb_start = sg.kb0;
+        if (first_seg) {
+          // Operand A of the first stages (weights in decode) does not depend on the previous
+          // kernel: fetch it before waiting for that kernel's results, then fetch B.
+          first_seg = false;
+          const int npre = min(p.stages, sg.kb1 - sg.kb0);
+          for (int i = 0; i < npre; ++i) {
+            mbar_arrive_expect_tx(&s.full[i], A_STAGE_BYTES + b_stage_bytes);
+            tma_load_2d(s.a + (size_t)i * A_STAGE_BYTES, &tmA, &s.full[i], (sg.kb0 + i) * BK, sg.tm * BM, pol_a);
+          }
+          griddep_wait();
+          if (trace) trace[1] = globaltimer_ns();
+          for (int i = 0; i < npre; ++i)
+            tma_load_2d(s.b + (size_t)i * b_stage_bytes, &tmB, &s.full[i], (sg.kb0 + i) * BK, sg.tn * p.bn, pol_b);
+          kb_start = sg.kb0 + npre;
+          stage = npre % p.stages;
+          phase = (npre == p.stages) ? 1u : 0u;
+        }
+        for (int kb = kb_start; kb < sg.kb1; ++kb) {
           if (!mbar_wait_bounded(&s.empty[stage], phase ^ 1, p.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag,
                                  WAIT_LIMIT_NS)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&s.full[stage], A_STAGE_BYTES + b_stage_bytes);
-          tma_load_2d(s.a + (size_t)stage * A_STAGE_BYTES, &tmA, &s.full[stage], kb * BK, un.tm * BM, pol_a);
-          tma_load_2d(s.b + (size_t)stage * b_stage_bytes, &tmB, &s.full[stage], kb * BK, un.tn * p.bn, pol_b);
+          tma_load_2d(s.a + (size_t)stage * A_STAGE_BYTES, &tmA, &s.full[stage], kb * BK, sg.tm * BM, pol_a);
+          tma_load_2d(s.b + (size_t)stage * b_stage_bytes, &tmB, &s.full[stage], kb * BK, sg.tn * p.bn, pol_b);
           if (++stage == p.stages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      if (first_seg) griddep_wait();  // no work: still order after the previous grid
+      if (trace) trace[2] = globaltimer_ns();
       if (!ok) {
         // drain: give copies already in flight a bounded chance to land before the CTA exits
         for (int i = 0; i < p.stages; ++i) {
@@ -325,8 +438,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++it) {
-      Unit un = decode_unit(u, p);
+    SegIter itr;
+    itr.init(p);
+    Seg sg;
+    while (ok && itr.next(p, sg)) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       int w = 1;
@@ -339,7 +454,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(acc * p.bn);
-      for (int kb = un.kb0; kb < un.kb1; ++kb) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
         if (lane == 0)
           w = mbar_wait_bounded(&s.full[stage], phase, p.err, ERR_MBAR_TIMEOUT_MMA, abort_flag, WAIT_LIMIT_NS);
         w = __shfl_sync(0xffffffffu, w, 0);
@@ -348,6 +463,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
+        if (trace && lane == 0 && it == 0 && kb == sg.kb0) trace[3] = globaltimer_ns();
         if (lane == 0) {
           const uint32_t a_addr = smem_u32(s.a + (size_t)stage * A_STAGE_BYTES);
           const uint32_t b_addr = smem_u32(s.b + (size_t)stage * b_stage_bytes);
@@ -356,7 +472,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // advance 16 bf16 = 32 bytes inside the swizzled 128-byte row: +2 in 16-byte units
-            umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, p.idesc, (kb > un.kb0 || k > 0) ? 1u : 0u);
+            umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, p.idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&s.empty[stage]);
         }
@@ -369,19 +485,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) break;
       if (lane == 0) umma_commit(&s.tfull[acc]);
       __syncwarp();
+      ++it;
     }
+    if (trace && lane == 0) trace[4] = globaltimer_ns();
   } else {
     // ------------------------------- epilogue (warps 2..5) -------------------------------
+    griddep_wait();  // output and workspace may still be in use by the previous grid
     const int et = threadIdx.x - 64;            // 0..127
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;        // accumulator row (TMEM lane)
-    float* slot0 = s.epi;
-    float* slot1 = s.epi + EPI_SLOT_FLOATS;
+    const uint32_t slot0 = smem_u32(s.epi);
+    const uint32_t slot1 = slot0 + EPI_SLOT_FLOATS * 4;
+    const size_t tile_floats = (size_t)BM * p.bn;
+    uint32_t fix_phase = 0;
     int it = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++it) {
-      Unit un = decode_unit(u, p);
+    SegIter itr;
+    itr.init(p);
+    Seg sg;
+    while (itr.next(p, sg)) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      ++it;
       if (et == 0)
         *s.epi_flag = mbar_wait_bounded(&s.tfull[acc], acc_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag,
                                         WAIT_LIMIT_NS);
@@ -389,10 +513,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int ok = *s.epi_flag;
       named_bar_sync(1, 128);
       if (!ok) break;
+      if (trace && et == 0 && it == 1) trace[5] = globaltimer_ns();
       tc_fence_after();
       const uint32_t taddr_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
 
-      if (p.splits == 1) {
+      if (sg.ncontrib == 1) {
         const int nsteps = ChunkPlan<EPI, TRANS>::steps(p.bn);
         for (int st = 0; st < nsteps; ++st) {
           int ca, cb, cw, cout;
@@ -404,69 +529,144 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_arrive(&s.tempty[acc]);
           }
           named_bar_sync(1, 128);
-          finalize_chunk<EPI, TRANS>(p, slot0, slot1, un.tm, un.tn, cout, cw, et);
+          finalize_chunk<EPI, TRANS>(p, slot0, slot1, sg.tm, sg.tn, cout, cw, et);
           named_bar_sync(1, 128);
         }
       } else {
-        // split-K: write this split's fp32 partial tile, then take a ticket
-        float* ws = p.workspace + ((size_t)un.split * tiles + un.tile) * (size_t)BM * p.bn;
-        for (int c = 0; c < p.bn; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr_row + c, r);
-          tmem_ld_wait();
-          float4* dst = reinterpret_cast<float4*>(ws + (size_t)row * p.bn + c);
+        // stream-K. The tile's owner is the CTA holding its first k-block (contributor 0); its
+        // segment of this tile is the last of its range, while the other contributors reach the
+        // tile first. Non-owners publish an fp32 partial and bump the tile counter; the owner waits
+        // (bounded) for all of them, adds the partials to its own TMEM accumulator in contributor
+        // order (deterministic) and runs the epilogue, then resets the counter for the next launch.
+        if (sg.contrib != 0) {
+          float* ws = p.workspace + (size_t)(sg.sk_tile + blockIdx.x) * tile_floats;
+          for (int c = 0; c < p.bn; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(taddr_row + c, r);
+            tmem_ld_wait();
+            float4* dst = reinterpret_cast<float4*>(ws + (size_t)row * p.bn + c);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-        }
-        tc_fence_before();
-        mbar_arrive(&s.tempty[acc]);
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (et == 0) {
-          int ticket = atomicAdd(&p.counters[un.tile], 1);
-          int last = (ticket == p.splits - 1);
-          if (last) p.counters[un.tile] = 0;
-          *s.epi_flag = last;
-        }
-        named_bar_sync(1, 128);
-        const int last = *s.epi_flag;
-        named_bar_sync(1, 128);
-        if (last) {
+            for (int i = 0; i < 4; ++i)
+              __stcg(dst + i, make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                          __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+          }
+          tc_fence_before();
+          mbar_arrive(&s.tempty[acc]);
+          if (trace && et == 0) trace[8] = globaltimer_ns();
           __threadfence();
+          named_bar_sync(1, 128);
+          if (et == 0) red_release_gpu_add(&p.counters[sg.sk_tile], 1);
+          if (trace && et == 0) trace[9] = globaltimer_ns();
+        } else {
+          // Owner: its segment of this tile is the last of its range, so the operand ring is idle.
+          // Pull the contributors' partial tiles into it with bulk copies (all in flight at once),
+          // then add them to the own accumulator chunk by chunk in contributor order.
+          const bool okw = wait_counter_eq(&p.counters[sg.sk_tile], sg.ncontrib - 1, WAIT_LIMIT_NS, p.err,
+                                           ERR_MBAR_TIMEOUT_EPILOGUE);
+          (void)okw;
+          named_bar_sync(1, 128);
+          if (et == 0) p.counters[sg.sk_tile] = 0;
+          if (trace && et == 0) trace[10] = globaltimer_ns();
+          const uint32_t tile_bytes = (uint32_t)(tile_floats * 4);
+          const size_t ring_bytes = (size_t)p.stages * (A_STAGE_BYTES + b_stage_bytes);
+          const int per_batch = (int)(ring_bytes / tile_bytes) < 1 ? 1 : (int)(ring_bytes / tile_bytes);
+          const float* part0 = p.workspace + (size_t)(sg.sk_tile + sg.first_cta) * tile_floats;
           const int nsteps = ChunkPlan<EPI, TRANS>::steps(p.bn);
-          const size_t split_stride = (size_t)tiles * BM * p.bn;
-          const float* ws0 = p.workspace + (size_t)un.tile * BM * p.bn;
+          // own accumulator chunks are kept in TMEM; partial batches accumulate into a running
+          // fp32 copy of the tile held in the ring when more than one batch is needed
+          const int nparts = sg.ncontrib - 1;
+          const int nbatch = (nparts + per_batch - 1) / per_batch;
           for (int st = 0; st < nsteps; ++st) {
             int ca, cb, cw, cout;
             ChunkPlan<EPI, TRANS>::step(st, p.bn, ca, cb, cw, cout);
-            for (int idx = et; idx < BM * cw; idx += 128) {
-              int r = idx / cw, c = idx - r * cw;
-              float a = 0.f, b = 0.f;
-              for (int sp = 0; sp < p.splits; ++sp) {
-                const float* w = ws0 + sp * split_stride + (size_t)r * p.bn;
-                a += __ldcg(w + ca + c);
-                if (cb >= 0) b += __ldcg(w + cb + c);
+            tmem_chunk_to_smem(taddr_row, ca, cw, slot0, row);
+            if (cb >= 0) tmem_chunk_to_smem(taddr_row, cb, cw, slot1, row);
+            if (st == nsteps - 1) {
+              tc_fence_before();
+              mbar_arrive(&s.tempty[acc]);
+            }
+            for (int bt_i = 0; bt_i < nbatch; ++bt_i) {
+              const int k0 = 1 + bt_i * per_batch;
+              const int kn = min(per_batch, nparts - bt_i * per_batch);
+              // the whole batch is re-fetched per chunk only when it cannot stay resident
+              const bool resident = (nbatch == 1);
+              if (!resident || st == 0) {
+                named_bar_sync(1, 128);  // ring free of the previous batch's readers
+                if (et == 0) {
+                  fence_proxy_async();
+                  mbar_arrive_expect_tx(s.fixbar, (uint32_t)kn * tile_bytes);
+                  for (int k = 0; k < kn; ++k)
+                    bulk_load(s.a + (size_t)k * tile_bytes, part0 + (size_t)(k0 + k) * tile_floats, tile_bytes,
+                              s.fixbar);
+                }
+                int okb = 1;
+                if (et == 0) {
+                  okb = mbar_wait_bounded(s.fixbar, fix_phase, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag,
+                                          WAIT_LIMIT_NS);
+                  *s.epi_flag = okb;
+                }
+                fix_phase ^= 1;
+                if (trace && et == 0 && st == 0) trace[12] = globaltimer_ns();
+                named_bar_sync(1, 128);
+              } else {
+                named_bar_sync(1, 128);
               }
-              slot0[r * EPI_LD + c] = a;
-              if (cb >= 0) slot1[r * EPI_LD + c] = b;
+              // add staged partials: a thread owns 4 consecutive columns of one row (16-byte shared
+              // loads; a warp covers 4 rows x 32 columns, conflict-free)
+              {
+                const uint32_t ring = smem_u32(s.a);
+                const uint32_t s0 = slot0, s1 = slot1;
+                const int q4 = cw >> 2;                 // float4 per row in this chunk (8 or 4)
+                const int q4s = (cw == 32) ? 3 : 2;     // log2(q4)
+                for (int v = et; v < BM * q4; v += 128) {
+                  const int r = v >> q4s, c = (v & (q4 - 1)) * 4;
+                  const uint32_t so = (uint32_t)(r * EPI_LD + c) * 4;
+                  float4 x0 = make_float4(lds_f32(s0 + so), lds_f32(s0 + so + 4), lds_f32(s0 + so + 8),
+                                          lds_f32(s0 + so + 12));
+                  float4 x1 = make_float4(0.f, 0.f, 0.f, 0.f);
+                  if (cb >= 0)
+                    x1 = make_float4(lds_f32(s1 + so), lds_f32(s1 + so + 4), lds_f32(s1 + so + 8),
+                                     lds_f32(s1 + so + 12));
+                  const uint32_t rowoff = (uint32_t)(r * p.bn) * 4;
+#pragma unroll 4
+                  for (int k = 0; k < kn; ++k) {
+                    const uint32_t pt = ring + (uint32_t)k * tile_bytes + rowoff;
+                    const float4 y = lds_f4(pt + (uint32_t)(ca + c) * 4);
+                    x0.x += y.x; x0.y += y.y; x0.z += y.z; x0.w += y.w;
+                    if (cb >= 0) {
+                      const float4 z = lds_f4(pt + (uint32_t)(cb + c) * 4);
+                      x1.x += z.x; x1.y += z.y; x1.z += z.z; x1.w += z.w;
+                    }
+                  }
+                  sts_f32(s0 + so, x0.x); sts_f32(s0 + so + 4, x0.y); sts_f32(s0 + so + 8, x0.z);
+                  sts_f32(s0 + so + 12, x0.w);
+                  if (cb >= 0) {
+                    sts_f32(s1 + so, x1.x); sts_f32(s1 + so + 4, x1.y); sts_f32(s1 + so + 8, x1.z);
+                    sts_f32(s1 + so + 12, x1.w);
+                  }
+                }
+              }
             }
             named_bar_sync(1, 128);
-            finalize_chunk<EPI, TRANS>(p, slot0, slot1, un.tm, un.tn, cout, cw, et);
+            if (trace && et == 0 && st == 0) trace[13] = globaltimer_ns();
+            finalize_chunk<EPI, TRANS>(p, slot0, slot1, sg.tm, sg.tn, cout, cw, et);
             named_bar_sync(1, 128);
+            if (trace && et == 0 && st == 0) trace[14] = globaltimer_ns();
           }
+          if (trace && et == 0) trace[11] = globaltimer_ns();
         }
       }
     }
   }
 
+  if (trace && threadIdx.x == 64) trace[6] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, p.tmem_cols);
   }
+  if (trace && threadIdx.x == 0) trace[7] = globaltimer_ns();
 }
 
 // ----------------------------------------------------------------------------------------------
@@ -499,7 +699,7 @@ static void launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const Gem
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     configured[dev] = true;
   }
-  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  launch_k(kern, dim3(grid), dim3(NUM_THREADS), smem, stream, ta, tb, p);
 }
 
 // Choose BN for a problem: decode (swap-AB) uses the token count rounded to 16, prefill 256 (or
@@ -513,21 +713,52 @@ int gemm_pick_bn(int N, int epi, bool trans) {
   return N >= 192 ? 256 : (N >= 96 ? 128 : ((N + 15) / 16 * 16));
 }
 
-int gemm_pick_splits(int M, int N, int K, int bn, int num_sms) {
-  int m_tiles = (M + BM - 1) / BM, n_tiles = (N + bn - 1) / bn;
-  int tiles = m_tiles * n_tiles;
-  int k_blocks = (K + BK - 1) / BK;
-  if (tiles >= num_sms / 2) return 1;
-  int splits = num_sms / tiles;
-  int max_splits = k_blocks / 2 > 0 ? k_blocks / 2 : 1;  // keep at least two k-blocks per split
-  if (splits > max_splits) splits = max_splits;
-  if (splits > 32) splits = 32;
-  return splits < 1 ? 1 : splits;
+// Schedule: whole tiles round-robin over a persistent grid for all but the last (partial) waves;
+// the remaining tiles' k-iterations are spread evenly over the grid (stream-K). Small problems
+// (fewer tiles than SMs) become pure stream-K, which replaces classic split-K.
+struct Plan {
+  int grid, dp_tiles, sk_iters, sk_tiles, tiles;
+  size_t ws_floats;
+};
+
+static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode) {
+  Plan pl{};
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + bn - 1) / bn;
+  const int kb = (K + BK - 1) / BK;
+  pl.tiles = m_tiles * n_tiles;
+  const long total_iters = (long)pl.tiles * kb;
+  int grid = num_sms;
+  if (force_mode == 1 || (force_mode == 0 && (pl.tiles % grid == 0 || pl.tiles >= 4 * grid))) {
+    // pure data-parallel persistent schedule
+    pl.grid = pl.tiles < grid ? pl.tiles : grid;
+    pl.dp_tiles = pl.tiles;
+    pl.sk_iters = 0;
+    pl.sk_tiles = 0;
+    pl.ws_floats = 0;
+    return pl;
+  }
+  int waves = pl.tiles / grid;
+  pl.dp_tiles = waves >= 2 ? (waves - 1) * grid : 0;
+  pl.sk_tiles = pl.tiles - pl.dp_tiles;
+  const long sk_total = (long)pl.sk_tiles * kb;
+  if (sk_total < grid) grid = (int)sk_total;
+  long w = (sk_total + grid - 1) / grid;
+  if (w < 2 && kb >= 2) {  // keep at least two k-blocks per stream-K share
+    w = 2;
+    grid = (int)((sk_total + w - 1) / w);
+  }
+  grid = (int)((sk_total + w - 1) / w);  // every CTA gets a non-empty share
+  pl.sk_iters = (int)w;
+  pl.grid = grid;
+  pl.ws_floats = (size_t)(pl.sk_tiles + grid) * BM * bn;
+  (void)total_iters;
+  return pl;
 }
 
 // out = A @ B^T (normal) or out^T = A @ B^T (trans). Returns nothing; errors go to `err`.
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn_req,
-                  int64_t splits_req, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err) {
+                  int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                  const c10::optional<at::Tensor>& trace) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm_tcgen05: tensors must be CUDA");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_tcgen05: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tcgen05: A [M,K], B [N,K]");
@@ -546,19 +777,22 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   TORCH_CHECK(bn % 16 == 0 && bn >= 16 && bn <= 256, "gemm_tcgen05: BN must be a multiple of 16 in [16,256]");
   if (epi == EPI_SILU_BF16 && !trans) TORCH_CHECK(bn % 128 == 0, "SiLU epilogue needs BN % 128 == 0");
   if (epi == EPI_SILU_BF16) TORCH_CHECK((trans ? M : N) % 128 == 0, "SiLU epilogue: feature dim % 128");
+  if (epi == EPI_ARGMAX)
+    TORCH_CHECK(trans && out.scalar_type() == at::kFloat && out.dim() == 3 && out.size(0) >= (M + BM - 1) / BM &&
+                    out.size(1) == N && out.size(2) == 2,
+                "argmax epilogue: swap-AB only, out float [m_tiles, N, 2]");
   p.bn = bn;
   p.m_tiles = (M + BM - 1) / BM;
   p.n_tiles = (N + bn - 1) / bn;
   p.k_blocks = (K + BK - 1) / BK;
   const int sms = num_sms_cached(dev);
-  int splits = splits_req > 0 ? (int)splits_req : gemm_pick_splits(M, N, K, bn, sms);
-  if (splits > p.k_blocks) splits = p.k_blocks;
-  p.splits = splits;
-  const int tiles = p.m_tiles * p.n_tiles;
-  if (splits > 1) {
-    TORCH_CHECK(workspace.numel() >= (int64_t)splits * tiles * BM * bn && workspace.scalar_type() == at::kFloat,
-                "gemm_tcgen05: workspace too small for split-K (need ", (int64_t)splits * tiles * BM * bn, " floats)");
-    TORCH_CHECK(counters.numel() >= tiles && counters.scalar_type() == at::kInt, "gemm_tcgen05: counters too small");
+  Plan pl = make_plan(M, N, K, bn, sms, (int)mode);
+  p.dp_tiles = pl.dp_tiles;
+  p.sk_iters_per_cta = pl.sk_iters;
+  if (pl.sk_tiles > 0) {
+    TORCH_CHECK(workspace.numel() >= (int64_t)pl.ws_floats && workspace.scalar_type() == at::kFloat,
+                "gemm_tcgen05: workspace too small for stream-K (need ", (int64_t)pl.ws_floats, " floats)");
+    TORCH_CHECK(counters.numel() >= pl.sk_tiles && counters.scalar_type() == at::kInt, "gemm_tcgen05: counters");
     p.workspace = workspace.data_ptr<float>();
     p.counters = counters.data_ptr<int>();
   }
@@ -567,15 +801,18 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   while (stages > 2 && gemm_smem_bytes(stages, bn) > budget) --stages;
   p.stages = stages;
   p.out = out.data_ptr();
-  p.ldo = out.stride(0);
+  p.ldo = epi == EPI_ARGMAX ? out.size(1) : out.stride(0);
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->numel() >= (int64_t)pl.grid * 16 && trace->scalar_type() == at::kLong, "gemm trace buffer");
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   p.err = err.data_ptr<int>();
   p.idesc = make_idesc_bf16(BM, bn);
   p.tmem_cols = tmem_cols_for(bn);
 
   CUtensorMap ta = tma_map_2d_bf16(A.data_ptr(), K, M, A.stride(0), BK, BM);
   CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, bn);
-  const int units = tiles * splits;
-  const int grid = units < sms ? units : sms;
+  const int grid = pl.grid;
   const size_t smem = gemm_smem_bytes(stages, bn);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   switch (epi * 2 + (trans ? 1 : 0)) {
@@ -585,21 +822,19 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
     case EPI_STORE_F32 * 2 + 1: launch_typed<EPI_STORE_F32, true>(ta, tb, p, grid, smem, stream); break;
     case EPI_SILU_BF16 * 2 + 0: launch_typed<EPI_SILU_BF16, false>(ta, tb, p, grid, smem, stream); break;
     case EPI_SILU_BF16 * 2 + 1: launch_typed<EPI_SILU_BF16, true>(ta, tb, p, grid, smem, stream); break;
+    case EPI_ARGMAX * 2 + 1: launch_typed<EPI_ARGMAX, true>(ta, tb, p, grid, smem, stream); break;
     default: TORCH_CHECK(false, "gemm_tcgen05: unknown epilogue ", epi);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// [bn, mode-independent workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters]
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device) {
   int bn = gemm_pick_bn((int)N, (int)epi, trans);
-  int sms = num_sms_cached((int)device);
-  int splits = gemm_pick_splits((int)M, (int)N, (int)K, bn, sms);
-  int kb = (int)((K + BK - 1) / BK);
-  if (splits > kb) splits = kb;
-  int tiles = (int)(((M + BM - 1) / BM) * ((N + bn - 1) / bn));
+  Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0);
   int stages = 8;
   while (stages > 2 && gemm_smem_bytes(stages, bn) > 232448) --stages;
-  return {bn, splits, (int64_t)splits * tiles * BM * bn, tiles, stages};
+  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, stages, pl.grid, pl.dp_tiles, pl.sk_iters};
 }
 
 }  // namespace mesh

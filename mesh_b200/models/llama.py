@@ -85,6 +85,9 @@ class LlamaRunner:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group)
         self._cand_gather = None
+        # keep fp32 logits (tests, sampling); the greedy decode path fuses argmax into the LM head
+        self.keep_logits = False
+        self.last_logits = None
 
     # ------------------------------------------------------------------------------------------
     def _resid_normed(self, T: int):
@@ -174,10 +177,15 @@ class LlamaRunner:
             torch.index_select(normed, 0, m.last_idx, out=final)
         else:
             final, S = normed, T
-        logits = buf("logits", (S, w.vocab_local), torch.float32)
-        ops.linear(final, w.lm_head, out=logits, epi=ops.EPI_STORE_F32)
         cand = buf("cand", (S, 2), torch.float32)
-        ops.argmax_partial(logits, w.vocab_start, cand)
+        if self.keep_logits or S > ops.SWAP_AB_MAX_TOKENS:
+            logits = buf("logits", (S, w.vocab_local), torch.float32)
+            ops.linear(final, w.lm_head, out=logits, epi=ops.EPI_STORE_F32)
+            ops.argmax_partial(logits, w.vocab_start, cand)
+            self.last_logits = logits
+        else:
+            tiles = buf("cand_tiles", ((w.vocab_local + 127) // 128, S, 2), torch.float32)
+            ops.lm_head_argmax(final, w.lm_head, w.vocab_start, tiles, cand)
         ids_out = buf("next_ids", (S,), torch.int32)
         if self.world == 1:
             ops.argmax_merge(cand.view(1, S, 2), ids_out)
@@ -185,5 +193,4 @@ class LlamaRunner:
             gathered = buf("cand_all", (self.world, S, 2), torch.float32)
             dist.all_gather_into_tensor(gathered.view(-1), cand.view(-1), group=self.group)
             ops.argmax_merge(gathered, ids_out)
-        self.last_logits = logits
         return ids_out

@@ -26,6 +26,7 @@ def _count(n: int = 1):
 EPI_STORE_BF16 = 0
 EPI_STORE_F32 = 1
 EPI_SILU_BF16 = 2
+EPI_ARGMAX = 3
 # decode-sized token counts use the swap-AB orientation (weights on the 128-row MMA side)
 SWAP_AB_MAX_TOKENS = 256
 
@@ -102,19 +103,30 @@ def scratch(device=None) -> DeviceScratch:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16, trans: bool = False,
-         bn: int = 0, splits: int = 0) -> torch.Tensor:
+         bn: int = 0, mode: int = 0, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = a @ b.T (trans=False, out [M, N']) or out^T = a @ b.T (trans=True, out [N, M'])
-    with the tcgen05 kernel. a [M, K], b [N, K] bf16 K-contiguous."""
+    with the tcgen05 kernel. a [M, K], b [N, K] bf16 K-contiguous. mode: 0 auto schedule,
+    1 whole tiles only, 2 stream-K for the tail waves."""
     s = scratch(a.device)
     M, N, K = a.shape[0], b.shape[0], a.shape[1]
-    plan = ext().gemm_plan(M, N, K, epi, trans, a.device.index)
-    bn_, splits_ = (bn or plan[0]), (splits or plan[1])
-    if splits_ > 1:
+    if mode == 0 and bn == 0:
+        key = (M, N, K, epi, trans, a.device.index)
+        plan = _PLANS.get(key)
+        if plan is None:
+            plan = _PLANS[key] = ext().gemm_plan(M, N, K, epi, trans, a.device.index)
+        if plan[2] > 0:
+            s.ensure_gemm(plan[1], plan[2])
+    else:
+        # explicit schedule (tests): size the workspace for the worst case of this shape
+        bn_ = bn or ext().gemm_plan(M, N, K, epi, trans, a.device.index)[0]
         tiles = ((M + 127) // 128) * ((N + bn_ - 1) // bn_)
-        s.ensure_gemm(splits_ * tiles * 128 * bn_, tiles)
-    ext().gemm_tcgen05(a, b, out, epi, trans, bn_, splits_, s.gemm_ws, s.gemm_counters, s.err)
+        s.ensure_gemm((tiles + s.num_sms) * 128 * bn_, tiles)
+    ext().gemm_tcgen05(a, b, out, epi, trans, bn, mode, s.gemm_ws, s.gemm_counters, s.err, trace)
     _count()
     return out
+
+
+_PLANS = {}
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, epi: int = EPI_STORE_BF16,
@@ -152,16 +164,22 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
 
 
 def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, window: int = 0,
-                splits: int = 0, max_len_hint: int = 0):
+                splits: int = 0, max_len_hint: int = 0, impl: str = "auto"):
+    """Paged GQA decode attention. impl: "tc" (TMA-streamed, tensor-core fragments; head_dim 128,
+    16-token pages), "simt" (CUDA-core variant, any page size, head_dim 64/128) or "auto"."""
     s = scratch(q.device)
-    B, hkv, D = q.shape[0], kcache.shape[1], kcache.shape[3]
+    B, hkv, ps, D = q.shape[0], kcache.shape[1], kcache.shape[2], kcache.shape[3]
     hq = q.shape[1] // D
+    if impl == "auto":
+        impl = "tc" if (D == 128 and ps == 16) else "simt"
     if splits <= 0:
-        splits = ext().attn_decode_pick_splits(B, hkv, max_len_hint or block_tables.shape[1] * kcache.shape[2],
-                                               s.num_sms)
+        splits = ext().attn_decode_pick_splits(B, hkv, max_len_hint or block_tables.shape[1] * ps, s.num_sms)
     if splits > 1:
         s.ensure_attn(B * hq * splits * (D + 1))
-    ext().attn_decode(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, splits, scale, window)
+    if impl == "tc":
+        ext().attn_decode_tc(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, s.err, splits, scale, window)
+    else:
+        ext().attn_decode(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, splits, scale, window)
     _count(2 if splits > 1 else 1)
     return out
 
@@ -175,6 +193,17 @@ def attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len: 
 
 def argmax_partial(logits: torch.Tensor, vocab_offset: int, out: torch.Tensor):
     ext().argmax_partial(logits, vocab_offset, out)
+    _count()
+    return out
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, vocab_offset: int, tiles_buf: torch.Tensor,
+                   out: torch.Tensor) -> torch.Tensor:
+    """Greedy head without materialising logits: the swap-AB GEMM epilogue keeps each token's max
+    over every 128-row vocabulary tile, then one kernel reduces the tiles. out: [T, 2] float
+    (value, global index bits)."""
+    gemm(w, x, tiles_buf, EPI_ARGMAX, trans=True)
+    ext().argmax_tiles(tiles_buf, vocab_offset, out)
     _count()
     return out
 

@@ -45,18 +45,18 @@ def test_gemm_bf16(M, N, K, trans):
     assert rel_err(out, want) < 1e-2
 
 
-@pytest.mark.parametrize("splits", [1, 2, 5])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("trans", [False, True])
-def test_gemm_f32_splitk(splits, trans):
+def test_gemm_f32_schedules(mode, trans):
     M, N, K = 64, 768, 2048
     x = _rand(M, K, seed=3)
     w = _rand(N, K, std=0.05, seed=4)
     want = x.float() @ w.float().T
     out = torch.empty(M, N, dtype=torch.float32, device=DEV)
     if trans:
-        ops.gemm(w, x, out, ops.EPI_STORE_F32, trans=True, splits=splits)
+        ops.gemm(w, x, out, ops.EPI_STORE_F32, trans=True, mode=mode)
     else:
-        ops.gemm(x, w, out, ops.EPI_STORE_F32, trans=False, splits=splits)
+        ops.gemm(x, w, out, ops.EPI_STORE_F32, trans=False, mode=mode)
     torch.cuda.synchronize()
     assert rel_err(out, want) < 2e-3
     # counters must be left at zero so graph replays and later calls work
@@ -74,6 +74,30 @@ def test_gemm_silu_mul(T):
     torch.cuda.synchronize()
     assert out.shape == (T, I)
     assert rel_err(out, want) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 6144, 4096), (1000, 1536, 512), (64, 28672, 1024)])
+@pytest.mark.parametrize("epi", [0, 2])
+def test_gemm_stream_k_matches_data_parallel(M, N, K, epi):
+    """Stream-K tail waves and whole-tile scheduling give identical results (fixed reduction order)."""
+    x = _rand(M, K, seed=14)
+    w = _rand(N, K, std=0.05, seed=15)
+    n_out = N // 2 if epi == 2 else N
+    o1 = torch.empty(M, n_out, dtype=torch.bfloat16, device=DEV)
+    o2 = torch.empty_like(o1)
+    trans = M <= 256
+    A, B = (w, x) if trans else (x, w)
+    ops.gemm(A, B, o1, epi, trans=trans, mode=1)
+    ops.gemm(A, B, o2, epi, trans=trans, mode=2)
+    torch.cuda.synchronize()
+    want = x.float() @ w.float().T
+    if epi == 2:
+        want = ref.silu_mul_interleaved(want)
+    assert rel_err(o1, want) < 1e-2 and rel_err(o2, want) < 1e-2
+    o3 = torch.empty_like(o1)
+    ops.gemm(A, B, o3, epi, trans=trans, mode=2)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, o3)  # deterministic
 
 
 def test_linear_both_orientations_agree():
@@ -179,10 +203,11 @@ def _paged_kv(lens, hkv, D, ps, seed):
     return kc, vc, bt.to(DEV), k_list, v_list
 
 
-@pytest.mark.parametrize("G,D", [(4, 128), (8, 128), (1, 128), (4, 64)])
+@pytest.mark.parametrize("G,D,impl", [(4, 128, "tc"), (8, 128, "tc"), (1, 128, "tc"), (2, 128, "tc"),
+                                      (4, 128, "simt"), (8, 128, "simt"), (4, 64, "simt")])
 @pytest.mark.parametrize("splits", [1, 3])
 @pytest.mark.parametrize("window", [0, 100])
-def test_attn_decode(G, D, splits, window):
+def test_attn_decode(G, D, impl, splits, window):
     lens = [1, 17, 300, 1029, 64]
     hkv, ps = 2, 16
     hq = hkv * G
@@ -190,7 +215,8 @@ def test_attn_decode(G, D, splits, window):
     q = _rand(len(lens), hq * D, seed=30)
     out = torch.empty_like(q)
     scale = 1 / math.sqrt(D)
-    ops.attn_decode(q, kc, vc, bt, torch.tensor(lens, dtype=torch.int32, device=DEV), out, scale, window, splits=splits)
+    ops.attn_decode(q, kc, vc, bt, torch.tensor(lens, dtype=torch.int32, device=DEV), out, scale, window, splits=splits,
+                    impl=impl)
     torch.cuda.synchronize()
     for i, L in enumerate(lens):
         want = ref.attention(q[i].view(1, hq, D), ks[i], vs[i], torch.tensor([L - 1], device=DEV),

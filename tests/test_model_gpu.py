@@ -29,6 +29,7 @@ def _rel(a, b):
 
 def test_prefill_and_decode_logits_match_oracle():
     cfg, wref, runner, dev = _setup()
+    runner.keep_logits = True
     prompt = [5, 77, 3, 900, 12, 1, 64, 255, 31, 8, 600, 2, 9, 14, 15, 16, 17, 300]
     T = len(prompt)
     pages = [3, 9]
@@ -77,6 +78,21 @@ def test_engine_generate_batch_consistency(graphs):
     assert together == alone
     assert all(len(o) == 6 for o in together)
     assert eng.alloc.num_used == 0  # all pages returned
+
+
+def test_fused_argmax_head_matches_logits_path():
+    cfg, wref, runner, dev = _setup()
+    x = torch.randn(37, cfg.hidden_dim, device=dev).to(torch.bfloat16)
+    from mesh_b200 import ops
+    w = runner.w
+    tiles = torch.empty((w.vocab_local + 127) // 128, 37, 2, device=dev)
+    cand = torch.empty(37, 2, device=dev)
+    ops.lm_head_argmax(x, w.lm_head, 0, tiles, cand)
+    logits = ops.linear(x, w.lm_head, epi=ops.EPI_STORE_F32)
+    torch.cuda.synchronize()
+    idx = cand[:, 1].contiguous().view(torch.int32)
+    assert idx.tolist() == logits.argmax(-1).tolist()
+    assert torch.allclose(cand[:, 0], logits.max(-1).values)
 
 
 def test_engine_matches_oracle_greedy_first_token():
