@@ -63,11 +63,6 @@ class SymmWorkspace:
         self.buf.zero_()
         torch.cuda.synchronize(device)
         gname = self.group.group_name
-        try:
-            if not symm_mem.is_symm_mem_enabled_for_group(gname):
-                symm_mem.enable_symm_mem_for_group(gname)
-        except Exception:
-            pass
         self.handle = symm_mem.rendezvous(self.buf, gname)
         ptrs: List[int] = list(self.handle.buffer_ptrs)
         if len(ptrs) != self.world:
@@ -103,6 +98,17 @@ class SymmWorkspace:
                                 self.rank, self.world, T, L.hidden, parity, gamma, eps, self.epoch, s.err,
                                 nblocks, two_shot, timeout_s)
         ops._count()
+
+    def reset(self):
+        """Collective: zero the flags and epoch counters on every rank. Needed after a timed-out
+        collective left the ranks' epochs out of step."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        self.buf[: self.layout.off_p0].zero_()
+        self.epoch.zero_()
+        ops.scratch(self.device).err.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
 
     def barrier(self, timeout_s: float = 5.0):
         s = ops.scratch(self.device)
