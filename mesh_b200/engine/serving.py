@@ -175,8 +175,6 @@ class Engine:
                seed_base: int = 0, eos_token: Optional[int] = None) -> int:
         if not prompt:
             raise ValueError("Cannot prefill an empty prompt without an explicit BOS policy")
-        if temperature > 0.0:
-            raise NotImplementedError("the CUDA-graph decode path samples greedily; use temperature=0")
         if len(prompt) + max_new_tokens > self.ecfg.max_seq_len:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.ecfg.max_seq_len}")
@@ -266,7 +264,27 @@ class Engine:
                      block_tables=torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True),
                      seq_lens=pin(klen, torch.int32), cu_q=pin(cu, torch.int32), last_idx=pin(last, torch.int64),
                      max_q_len=max(b - a for _, a, b in items), decode=False)
-        next_ids = self.runner.forward(m)
+        sampled = [i for i, (s, a, b) in enumerate(items) if s.temperature > 0.0 and b == len(s.prompt)]
+        r = self.runner
+        if sampled:
+            r.keep_logits = True
+        try:
+            next_ids = r.forward(m)
+        finally:
+            r.keep_logits = False
+        if sampled:
+            import torch.distributed as dist
+            from ..ops.sampling import sample
+            logits = r.last_logits
+            if r.world > 1:
+                parts = [torch.empty_like(logits) for _ in range(r.world)]
+                dist.all_gather(parts, logits.contiguous(), group=r.group)
+                logits = torch.cat(parts, -1)[:, :self.cfg.vocab_size]
+            next_ids = next_ids.clone()
+            for i in sampled:
+                s_ = items[i][0]
+                next_ids[i] = sample(logits[i:i + 1], s_.temperature, s_.top_p,
+                                     [s_.seed_base ^ len(s_.prompt)]).to(torch.int32)[0]
         finished_prompts = []
         rows, slots = [], []
         for i, (s, a, b) in enumerate(items):
@@ -296,11 +314,15 @@ class Engine:
         return finished_prompts
 
     # ----------------------------------------------------------------------------- decode
-    def decode_step(self) -> int:
-        """One decode step over all sessions in the decode phase; returns the batch size."""
-        act = [s for s in self.running if s is not None and s.status == "decoding"]
+    def decode_step(self, only=None) -> int:
+        """One decode step over the sessions in the decode phase (all of them, or the ``only``
+        subset chosen by a microbatch planner); returns the batch size."""
+        act = [s for s in self.running if s is not None and s.status == "decoding"
+               and (only is None or s.sid in only)]
         if not act:
             return 0
+        if any(s.temperature > 0.0 for s in act):
+            return self._decode_step_sampled(act)
         hi = max(s.slot for s in act) + 1
         b = self.dec.bucket_for(hi)
         pos = np.zeros(b, dtype=np.int32)
@@ -313,6 +335,14 @@ class Engine:
             seq[s.slot] = p + 1
             slot[s.slot] = s.pages[p // self.page_size] * self.page_size + p % self.page_size
         d = self.dec
+        partial = only is not None and any(
+            s is not None and s.status == "decoding" and s.slot < b and s not in act for s in self.running)
+        if partial:
+            keep_ids = d.ids[:b].clone()
+            mask = torch.zeros(b, dtype=torch.bool)
+            for s in act:
+                mask[s.slot] = True
+            mask = mask.pin_memory().to(self.device, non_blocking=True)
         d.pos[:b].copy_(torch.from_numpy(pos).pin_memory(), non_blocking=True)
         d.seq_lens[:b].copy_(torch.from_numpy(seq).pin_memory(), non_blocking=True)
         d.slot[:b].copy_(torch.from_numpy(slot).pin_memory(), non_blocking=True)
@@ -320,6 +350,8 @@ class Engine:
             d.block_tables.copy_(torch.from_numpy(self.bt_host).pin_memory(), non_blocking=True)
             self.bt_dirty = False
         d.step(b)
+        if partial:
+            d.ids[:b].copy_(torch.where(mask, d.ids[:b], keep_ids))
         row = len(self.hist_rows)
         if row >= self.history.shape[0]:
             self.flush_history()
@@ -339,6 +371,56 @@ class Engine:
             if s.done:
                 self._retire(s)
         return len(act)
+
+    def _decode_step_sampled(self, act) -> int:
+        """Decode step with temperature/top-p sampling: eager forward keeping fp32 logits, gathered
+        across TP ranks, then the reference's seeded device sampler."""
+        import torch.distributed as dist
+        from ..ops.sampling import sample
+        from ..models.llama import StepMeta
+        n = len(act)
+        pos, seq, slot, bt = [], [], [], np.zeros((n, self.max_pages_per_seq), dtype=np.int32)
+        for i, s in enumerate(act):
+            p = s.kv_len
+            self._ensure_pages(s, p + 1)
+            pos.append(p)
+            seq.append(p + 1)
+            slot.append(s.pages[p // self.page_size] * self.page_size + p % self.page_size)
+            bt[i, :len(s.pages)] = s.pages
+        dev = self.device
+        ids = torch.stack([self.dec.ids[s.slot] for s in act])
+        m = StepMeta(ids=ids, pos=torch.tensor(pos, dtype=torch.int32, device=dev),
+                     slot=torch.tensor(slot, dtype=torch.int64, device=dev),
+                     block_tables=torch.from_numpy(bt).to(dev), seq_lens=torch.tensor(seq, dtype=torch.int32, device=dev),
+                     max_q_len=self.max_pages_per_seq * self.page_size, decode=True)
+        r = self.runner
+        r.keep_logits = True
+        try:
+            r.forward(m)
+        finally:
+            r.keep_logits = False
+        logits = r.last_logits
+        if r.world > 1:
+            parts = [torch.empty_like(logits) for _ in range(r.world)]
+            dist.all_gather(parts, logits.contiguous(), group=r.group)
+            logits = torch.cat(parts, -1)[:, :self.cfg.vocab_size]
+        toks = []
+        for i, s in enumerate(act):
+            seed = s.seed_base ^ (s.kv_len + 1)
+            toks.append(sample(logits[i:i + 1], s.temperature, s.top_p, [seed]))
+        toks = torch.cat(toks).to(torch.int32)
+        for i, s in enumerate(act):
+            self.dec.ids[s.slot] = toks[i]
+            s.kv_len += 1
+            s.n_generated += 1
+            s.decode_steps_served += 1
+        self.hist_first.append(([s.sid for s in act], toks))
+        self.stats["decode_tokens"] += n
+        self.stats["decode_steps"] += 1
+        for s in act:
+            if s.done:
+                self._retire(s)
+        return n
 
     def _retire(self, s: Session):
         s.status = "finished"

@@ -29,12 +29,14 @@ ext_modules = [
         extra_compile_args={"cxx": CXX, "nvcc": NVCC},
     ),
 ]
-if os.path.exists(os.path.join(ROOT, "csrc", "runtime", "runtime.cpp")):
-    ext_modules.append(CppExtension(
-        name="mesh_b200._runtime",
-        sources=["csrc/runtime/runtime.cpp"],
-        extra_compile_args={"cxx": CXX},
-    ))
+from pybind11.setup_helpers import Pybind11Extension  # noqa: E402
+
+ext_modules.append(Pybind11Extension(
+    "mesh_b200._runtime",
+    sources=["csrc/runtime/runtime.cpp"],
+    extra_compile_args=CXX,
+    cxx_std=17,
+))
 
 setup(
     name="mesh_b200",
