@@ -355,7 +355,9 @@ class InferenceCoordinator:
             while sid in self.sessions:
                 self.step()
         except Exception as e:  # surface as a failed result like the reference
+            import traceback
             self.stats.add("jobs_failed")
+            e = RuntimeError(f"{e}\n{traceback.format_exc()}")
             if sid in self.sessions:
                 s = self.sessions.pop(sid)
                 self.sched.drop(s.handle)

@@ -33,7 +33,7 @@ def sample(logits: torch.Tensor, temperature: float, top_p: float, seeds: Sequen
         cdf = probs.cumsum(-1)
         crossing = (cdf >= thr).to(torch.int32)
         return crossing.argmax(-1)
-    sp, si = probs.sort(-1, descending=True, stable=True)
+    sp, si = probs.sort(dim=-1, descending=True, stable=True)
     keep = (sp.cumsum(-1) - sp) < top_p
     f = torch.where(keep, sp, torch.zeros_like(sp))
     f = f * (1.0 / f.sum(-1, keepdim=True))

@@ -50,8 +50,11 @@ def test_gpu_first_token_matches_cpu_oracle_and_sampling_is_seeded():
     assert g == c
     r1, r2 = _req(p, 6, 0.9, 0.9), _req(p, 6, 0.9, 0.9)
     r2.job_id = r1.job_id  # same seed base -> same samples
-    a = InferenceCoordinator(GpuBackend(eng)).process_inference(r1).generated_tokens
-    b = InferenceCoordinator(GpuBackend(eng)).process_inference(r2).generated_tokens
+    ra = InferenceCoordinator(GpuBackend(eng)).process_inference(r1)
+    assert ra.success, ra.error
+    rb = InferenceCoordinator(GpuBackend(eng)).process_inference(r2)
+    assert rb.success, rb.error
+    a, b = ra.generated_tokens, rb.generated_tokens
     assert a == b and len(a) == 6
     eng.close()
 

@@ -147,3 +147,16 @@ def test_sliding_window_trims_oldest():
     assert f.k_cache[0].shape[0] == 4
     f.decode_step(7)
     assert f.k_cache[0].shape[0] == 4
+
+
+def test_torch_sampler_matches_device_semantics_oracle():
+    import torch
+    from mesh_b200.ops.sampling import sample
+    rng = np.random.default_rng(9)
+    for trial in range(40):
+        logits = (rng.standard_normal((3, 50)) * 2.5).astype(np.float32)
+        seeds = [trial * 31 + i for i in range(3)]
+        for temp, top_p in [(1.0, 1.0), (0.7, 0.9), (1.3, 0.3), (0.0, 0.9)]:
+            got = sample(torch.from_numpy(logits), temp, top_p, seeds).tolist()
+            want = T.sample_tokens_device_semantics(logits, temp, top_p, seeds)
+            assert got == want, (trial, temp, top_p)
