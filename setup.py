@@ -44,4 +44,6 @@ setup(
     packages=["mesh_b200"],
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={"console_scripts": ["mesh=mesh_b200.cli.main:main",
+                                      "mesh-control-plane=mesh_b200.control_plane.app:main"]},
 )
