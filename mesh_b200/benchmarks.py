@@ -1,0 +1,324 @@
+"""Benchmarks of the BASELINE configurations other than the headline (``bench.py`` runs config #2).
+
+    python -m mesh_b200.benchmarks cpu-tp2            # config #1: TinyLlama, cpu, TP=2 over loopback
+    torchrun ... -m mesh_b200.benchmarks prefill      # config #3: 2k/8k/32k single-sequence prefill (TTFT)
+    torchrun ... -m mesh_b200.benchmarks allreduce    # config #5: fused AR+norm vs NCCL vs host ring
+    torchrun ... -m mesh_b200.benchmarks serve70b     # config #4: 70B TP=8, 256 sessions, 10% KV handoff
+
+Every GPU number is timed with CUDA events on the launching stream after warm-up and reported as
+the max over ranks; rank 0 prints one JSON line per measurement.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import time
+
+import numpy as np
+
+
+# ------------------------------------------------------------------------------------------ config 1
+def _cpu_rank(rank, ports, out_q, prompt, gen, seed):
+    from .config import get_preset
+    from .models.sharding import shard_layout
+    from .models.weights import synthetic_reference_weights
+    from .oracle.tp_forward import ShardedForwardPass, shard_reference_weights
+    from .parallel.tcp_plane import TensorPlane, WorkerRing
+    cfg = get_preset("tinyllama-1.1b")
+    plane = TensorPlane(port=ports[rank])
+    addrs = [("127.0.0.1", p) for p in ports]
+    w = synthetic_reference_weights(cfg, seed=seed)
+    lay = shard_layout(cfg, rank, 2)
+    fp = ShardedForwardPass(cfg, lay, shard_reference_weights(w, lay), WorkerRing(plane, rank, addrs, timeout_s=600))
+    del w
+    fp.ring.barrier()
+    t0 = time.perf_counter()
+    toks = fp.generate(prompt, gen)
+    dt = time.perf_counter() - t0
+    out_q.put((rank, toks, dt, fp.ring.time_ms, fp.ring.operations))
+    fp.ring.barrier()
+    plane.close()
+
+
+def _free_ports(n):
+    import socket
+    socks, ports = [], []
+    for _ in range(n):
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        socks.append(s)
+        ports.append(s.getsockname()[1])
+    for s in socks:
+        s.close()
+    return ports
+
+
+def cpu_tp2(args):
+    import multiprocessing as mp
+    from .config import get_preset
+    from .models.weights import synthetic_reference_weights
+    from .oracle.forward import LocalForwardPass
+    rng = np.random.default_rng(args.seed)
+    cfg = get_preset("tinyllama-1.1b")
+    prompt = rng.integers(0, cfg.vocab_size, 32).tolist()
+    ctx = mp.get_context("spawn")
+    oq = ctx.Queue()
+    ports = _free_ports(2)
+    ps = [ctx.Process(target=_cpu_rank, args=(r, ports, oq, prompt, args.gen, args.seed)) for r in range(2)]
+    [p.start() for p in ps]
+    res = sorted(oq.get(timeout=3600) for _ in range(2))
+    [p.join() for p in ps]
+    tp_dt = max(r[2] for r in res)
+    w = synthetic_reference_weights(cfg, seed=args.seed)
+    t0 = time.perf_counter()
+    ref = LocalForwardPass(w).generate(prompt, args.gen)
+    base_dt = time.perf_counter() - t0
+    print(json.dumps({"config": "tinyllama-1.1b cpu tp2 loopback, prompt 32, greedy 16",
+                      "tp2_tokens_per_s": args.gen / tp_dt, "tp2_seconds": tp_dt,
+                      "allreduce_ms_per_rank": res[0][3], "allreduce_ops": res[0][4],
+                      "oracle_tokens_per_s": args.gen / base_dt, "oracle_seconds": base_dt,
+                      "tokens_match_oracle": res[0][1] == ref == res[1][1]}))
+
+
+# ------------------------------------------------------------------------------------------ GPU helpers
+def _dist():
+    import torch
+    import torch.distributed as dist
+    from .parallel import dist as mdist
+    di = mdist.init(timeout_s=300.0)
+    return di, dist, torch
+
+
+def _max_over_ranks(x, dist, torch, dev):
+    t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    if dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------ config 3
+def prefill(args):
+    di, dist, torch = _dist()
+    from .config import EngineConfig, get_preset
+    from .models.llama import KVPool, LlamaRunner, StepMeta
+    from .models.weights import synthetic_device_weights
+    cfg = get_preset(args.model)
+    dev = di.device
+    maxlen = max(args.lengths)
+    chunk = args.chunk
+    w = synthetic_device_weights(cfg, di.rank, di.world, device=dev)
+    pages = maxlen // 16 + 8
+    kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
+    ecfg = EngineConfig(max_seq_len=maxlen + 16, tp=di.world)
+    runner = LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD if di.world > 1 else None,
+                         max_tokens=chunk, max_pos=maxlen + 16)
+    bt = torch.arange(1, pages, device=dev, dtype=torch.int32)[None]
+    g = torch.Generator().manual_seed(1)
+    for L in args.lengths:
+        ids_all = torch.randint(0, cfg.vocab_size, (L,), generator=g, dtype=torch.int32).to(dev)
+
+        def run():
+            nxt = None
+            for a in range(0, L, chunk):
+                b = min(L, a + chunk)
+                pos = torch.arange(a, b, device=dev, dtype=torch.int32)
+                m = StepMeta(ids=ids_all[a:b], pos=pos, slot=(bt[0, pos.long() // 16].long() * 16 + pos.long() % 16),
+                             block_tables=bt, seq_lens=torch.tensor([b], device=dev, dtype=torch.int32),
+                             cu_q=torch.tensor([0, b - a], device=dev, dtype=torch.int32),
+                             last_idx=torch.tensor([b - a - 1], device=dev), max_q_len=b - a, decode=False)
+                nxt = runner.forward(m)
+            return nxt
+
+        for _ in range(args.warmup):
+            run()
+        torch.cuda.synchronize()
+        if di.world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            run()
+        e.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(s.elapsed_time(e) / args.steps, dist, torch, dev)
+        flops = 2.0 * cfg.param_count() * L + 2.0 * cfg.num_layers * cfg.hidden_dim * L * L  # GEMMs + causal attn
+        if di.rank == 0:
+            print(json.dumps({"config": f"{args.model} prefill L={L} batch 1 tp{di.world}", "ttft_ms": ms,
+                              "prefill_tokens_per_s": L / (ms / 1e3), "model_tflops": flops / (ms / 1e3) / 1e12,
+                              "chunk_tokens": chunk}), flush=True)
+    from .parallel import dist as mdist
+    mdist.shutdown()
+
+
+# ------------------------------------------------------------------------------------------ config 5
+def allreduce(args):
+    di, dist, torch = _dist()
+    from . import ops
+    from .parallel.symm import SymmWorkspace
+    dev = di.device
+    Hs = args.hidden
+    Ts = args.tokens
+    tmax = max(Ts)
+    results = []
+    for H in Hs:
+        ws = SymmWorkspace(tmax, H, dev)
+        gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        for T in Ts:
+            part = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            resid = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            nrm = torch.empty_like(resid)
+            ws.partial(0, T).copy_(part)
+            ws.partial(1, T).copy_(part)
+            ws.resid(T).copy_(resid)
+
+            def timed(fn, iters):
+                for i in range(3):
+                    fn(i)
+                torch.cuda.synchronize()
+                dist.barrier()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                for i in range(iters):
+                    fn(i)
+                e.record()
+                torch.cuda.synchronize()
+                return _max_over_ranks(s.elapsed_time(e) * 1e3 / iters, dist, torch, dev)
+
+            row = {"T": T, "H": H, "world": di.world}
+            for mode in ("oneshot", "twoshot"):
+                row[f"fused_{mode}_us"] = timed(
+                    lambda i, m=mode: ws.fused_allreduce_norm(T, i & 1, gamma, 1e-5, two_shot=(m == "twoshot")), 20)
+            buf = part.clone()
+            r2 = resid.clone()
+            row["nccl_plus_norm_us"] = timed(
+                lambda i: (dist.all_reduce(buf), ops.add_rmsnorm(r2, gamma, nrm, 1e-5, delta=buf)), 20)
+            if T * H <= 64 * 4096:
+                # the reference's algorithm: device -> host, ring over TCP, host -> device
+                from .parallel.tcp_plane import TensorPlane, WorkerRing
+                if not hasattr(allreduce, "_ring"):
+                    plane = TensorPlane()
+                    addrs = [None] * di.world
+                    dist.all_gather_object(addrs, plane.addr)
+                    allreduce._ring = WorkerRing(plane, di.rank, addrs)
+                ring = allreduce._ring
+
+                def host_ring(i):
+                    x = part.float().cpu().numpy()
+                    y = ring.all_reduce(x)
+                    torch.from_numpy(y).to(dev)
+                row["host_tcp_ring_us"] = timed(host_ring, 5)
+            best = min(row["fused_oneshot_us"], row["fused_twoshot_us"])
+            nbytes = 2 * T * H * 2 * (di.world - 1) / di.world  # ring-equivalent bytes per rank
+            row["fused_busbw_GBps"] = nbytes / (best * 1e-6) / 1e9
+            row["speedup_vs_nccl"] = row["nccl_plus_norm_us"] / best
+            results.append(row)
+            if di.rank == 0:
+                print(json.dumps(row), flush=True)
+        del ws
+    from .parallel import dist as mdist
+    mdist.shutdown()
+
+
+# ------------------------------------------------------------------------------------------ config 4
+def serve70b(args):
+    """256 sessions, prompts U[128,2048], 256 output tokens; after half the decode steps 10% of
+    the sessions are handed off (KV snapshot out, session released, snapshot re-imported as a new
+    session) to exercise checkpoint-backed KV handoff between decode queues."""
+    di, dist, torch = _dist()
+    from .config import EngineConfig, get_preset
+    from .engine.kv_snapshot import KVSequenceState, export_snapshot, import_snapshot
+    from .engine.serving import Engine
+    from .models.llama import KVPool, LlamaRunner
+    from .models.weights import synthetic_device_weights
+    cfg = get_preset(args.model)
+    if args.layers:
+        cfg = cfg.replace(num_layers=args.layers)
+    dev = di.device
+    S, G = args.sessions, args.gen
+    rng = np.random.default_rng(7)
+    lens = rng.integers(128, 2049, S).tolist()
+    maxs = (2048 + G + 15) // 16 * 16
+    ecfg = EngineConfig(tp=di.world, max_seq_len=maxs, prefill_chunk_tokens=args.chunk)
+    w = synthetic_device_weights(cfg, di.rank, di.world, device=dev)
+    pages = sum((l + G + 15) // 16 for l in lens) + 64
+    kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
+    runner = LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD if di.world > 1 else None,
+                         max_tokens=args.chunk + 2048)
+    eng = Engine(runner, ecfg, max_batch=S)
+    prompts = [rng.integers(0, cfg.vocab_size, l).tolist() for l in lens]
+    ev0, evp, evd = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    ev0.record()
+    sids = [eng.submit(p, G) for p in prompts]
+    while eng.waiting:
+        eng.prefill_step()
+    evp.record()
+    steps = 0
+    handed = 0
+    while eng.has_work():
+        eng.decode_step()
+        steps += 1
+        if steps == G // 2 and args.handoff > 0:
+            # mid-run handoff of a fraction of the sessions between decode queues
+            n = max(1, int(args.handoff * S))
+            for sid in sids[:n]:
+                s = eng.sessions[sid]
+                if s.status != "decoding":
+                    continue
+                snap = export_snapshot(kv.k, kv.v, s.pages, KVSequenceState(0, s.kv_len, s.kv_len), cfg.name)
+                blob = snap.to_bytes()
+                eng._free_session(s)
+                from .engine.kv_snapshot import KVCacheSnapshot
+                s.pages = import_snapshot(kv.k, kv.v, eng.alloc, KVCacheSnapshot.from_bytes(blob))
+                free = eng._free_slots()
+                s.slot = free[0]
+                eng.running[s.slot] = s
+                eng.bt_host[s.slot, :len(s.pages)] = s.pages
+                eng.bt_dirty = True
+                handed += 1
+    evd.record()
+    eng.flush_history()
+    torch.cuda.synchronize()
+    dec_ms = _max_over_ranks(evp.elapsed_time(evd), dist, torch, dev)
+    pre_ms = _max_over_ranks(ev0.elapsed_time(evp), dist, torch, dev)
+    ttft = sorted(ev0.elapsed_time(eng.sessions[s].ttft_event) for s in sids)
+    p50 = _max_over_ranks(ttft[len(ttft) // 2], dist, torch, dev)
+    if di.rank == 0:
+        print(json.dumps({"config": f"{cfg.name} tp{di.world} {S} sessions U[128,2048] x {G}",
+                          "decode_tokens_per_s": S * (G - 1) / (dec_ms / 1e3), "p50_ttft_ms": p50,
+                          "prefill_ms": pre_ms, "decode_ms": dec_ms, "sessions_handed_off": handed,
+                          "layers": cfg.num_layers}), flush=True)
+    eng.close()
+    from .parallel import dist as mdist
+    mdist.shutdown()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c1 = sub.add_parser("cpu-tp2")
+    c1.add_argument("--gen", type=int, default=16)
+    c1.add_argument("--seed", type=int, default=0)
+    c3 = sub.add_parser("prefill")
+    c3.add_argument("--model", default="llama3-8b")
+    c3.add_argument("--lengths", type=int, nargs="+", default=[2048, 8192, 32768])
+    c3.add_argument("--chunk", type=int, default=8192)
+    c3.add_argument("--steps", type=int, default=3)
+    c3.add_argument("--warmup", type=int, default=2)
+    c5 = sub.add_parser("allreduce")
+    c5.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 4096, 8192])
+    c5.add_argument("--hidden", type=int, nargs="+", default=[4096, 8192])
+    c4 = sub.add_parser("serve70b")
+    c4.add_argument("--model", default="llama3-70b")
+    c4.add_argument("--sessions", type=int, default=256)
+    c4.add_argument("--gen", type=int, default=256)
+    c4.add_argument("--chunk", type=int, default=8192)
+    c4.add_argument("--handoff", type=float, default=0.1)
+    c4.add_argument("--layers", type=int, default=0)
+    a = ap.parse_args()
+    {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    main()
