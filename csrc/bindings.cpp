@@ -4,7 +4,7 @@
 namespace mesh {
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn,
                   int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
-                  const c10::optional<at::Tensor>& trace);
+                  const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device);
 void add_rmsnorm(const c10::optional<at::Tensor>& delta, at::Tensor& resid, const at::Tensor& gamma, at::Tensor& normed,
                  double eps);
@@ -32,13 +32,18 @@ void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, i
 void ar_barrier(const at::Tensor& bases, int64_t off_flags, int64_t rank, int64_t world, at::Tensor& epoch,
                 at::Tensor& err, double timeout_s, const at::Tensor& device_ref);
 int64_t ar_flags_bytes();
+void ar_push_reduce_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_push, int64_t off_resid,
+                         int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t t_max, int64_t H,
+                         const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
+                         bool two_shot, double timeout_s);
 }  // namespace mesh
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mesh_b200 sm_100a kernels";
   m.def("gemm_tcgen05", &mesh::gemm_tcgen05, "tcgen05 GEMM out = A @ B^T (or its transpose)", py::arg("A"),
         py::arg("B"), py::arg("out"), py::arg("epi"), py::arg("trans"), py::arg("bn"), py::arg("mode"),
-        py::arg("workspace"), py::arg("counters"), py::arg("err"), py::arg("trace") = py::none());
+        py::arg("workspace"), py::arg("counters"), py::arg("err"), py::arg("trace") = py::none(),
+        py::arg("push") = std::vector<int64_t>{});
   m.def("gemm_plan", &mesh::gemm_plan, "tile plan [bn, workspace_floats, stream-K tiles, stages, grid, dp_tiles, sk_iters]");
   m.def("add_rmsnorm", &mesh::add_rmsnorm, "resid += delta; normed = rmsnorm(resid) * gamma");
   m.def("rope_kv_write", &mesh::rope_kv_write, "RoPE on q/k + paged KV write");
@@ -53,4 +58,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");
   m.def("ar_barrier", &mesh::ar_barrier, "bounded cross-rank barrier over peer flags");
   m.def("ar_flags_bytes", &mesh::ar_flags_bytes, "bytes of the flag region of the AR workspace");
+  m.def("ar_push_reduce_norm", &mesh::ar_push_reduce_norm,
+        "reduce the partial tiles peers pushed into this rank (+residual, RMSNorm, all-gather)");
 }

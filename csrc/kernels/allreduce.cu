@@ -21,6 +21,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+
 #include "../include/sm100.cuh"
 #include "../include/launch.h"
 
@@ -41,6 +43,11 @@ struct ArArgs {
   uint32_t* epoch;              // local [AR_MAX_BLOCKS]
   int* err;
   uint64_t timeout_ns;
+  // fused reduce-scatter mode: the GEMMs of all ranks pushed their bf16 partial rows into this
+  // rank's slots [world][t_max][H] at off_push; reduction reads local memory only
+  int push;
+  long off_push;
+  int t_max;
 };
 
 __device__ __forceinline__ uint32_t* flag_ptr(const ArArgs& a, int peer, int phase, int block, int src) {
@@ -78,7 +85,9 @@ __device__ __forceinline__ void reduce_norm_row(const ArArgs& a, long row, float
       for (int j = 0; j < 4; ++j) unpack_bf16x2(ru[j], x[i][2 * j], x[i][2 * j + 1]);
       for (int p = 0; p < a.world; ++p) {
         const __nv_bfloat16* src =
-            reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H + v * 8;
+            a.push ? reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_push) +
+                         ((long)p * a.t_max + row) * a.H + v * 8
+                   : reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H + v * 8;
         uint4 d = __ldcg(reinterpret_cast<const uint4*>(src));
         const uint32_t* du = reinterpret_cast<const uint32_t*>(&d);
 #pragma unroll
@@ -138,7 +147,108 @@ __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long ro
   }
 }
 
-template <int MAXV, bool TWO_SHOT>
+// Warp-per-row reduction: each warp owns one token row at a time. Pass 1 sums the residual and the
+// sources chunk by chunk (two 16-byte chunks per lane in flight per source), stores the bf16 residual
+// (locally, and into every rank for two-shot) and accumulates the sum of squares; pass 2 re-reads the
+// residual it just wrote and stores the normalised row. No block-wide synchronisation per row, so
+// thousands of rows are in flight and remote-load latency overlaps.
+__device__ __forceinline__ const uint4* src_row(const ArArgs& a, int p, long row) {
+  const __nv_bfloat16* s =
+      a.push ? reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_push) + ((long)p * a.t_max + row) * a.H
+             : reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H;
+  return reinterpret_cast<const uint4*>(s);
+}
+
+template <bool TWO_SHOT>
+__device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, int lane) {
+  const int nvec = a.H / 8;
+  uint4* resid_l = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[a.rank] + a.off_resid) + row * a.H);
+  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
+  float ss = 0.f;
+  constexpr int U = 2;
+  for (int c0 = lane; c0 < nvec; c0 += 32 * U) {
+    float acc[U][8];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 32;
+      ok[u] = c < nvec;
+      if (ok[u]) {
+        uint4 r = resid_l[c];
+        const uint32_t* ru = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) unpack_bf16x2(ru[j], acc[u][2 * j], acc[u][2 * j + 1]);
+      }
+    }
+    for (int p = 0; p < a.world; ++p) {
+      const uint4* sr = src_row(a, p, row);
+      uint4 d[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (ok[u]) d[u] = __ldcg(sr + c0 + u * 32);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!ok[u]) continue;
+        const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float x0, x1;
+          unpack_bf16x2(du[j], x0, x1);
+          acc[u][2 * j] += x0;
+          acc[u][2 * j + 1] += x1;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (!ok[u]) continue;
+      uint4 o;
+      uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ou[j] = pack_bf16x2(acc[u][2 * j], acc[u][2 * j + 1]);
+        float r0, r1;
+        unpack_bf16x2(ou[j], r0, r1);  // normalise the stored (bf16-rounded) residual
+        ss += r0 * r0 + r1 * r1;
+      }
+      const int c = c0 + u * 32;
+      if (TWO_SHOT) {
+        for (int q = 0; q < a.world; ++q)
+          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[q] + a.off_resid) + row * a.H)[c] = o;
+      } else {
+        resid_l[c] = o;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / (float)a.H + a.eps);
+  for (int c = lane; c < nvec; c += 32) {
+    uint4 r = resid_l[c];
+    uint4 g = gv[c];
+    const uint32_t* ru = reinterpret_cast<const uint32_t*>(&r);
+    const uint32_t* gu = reinterpret_cast<const uint32_t*>(&g);
+    uint4 o;
+    uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float r0, r1, g0, g1;
+      unpack_bf16x2(ru[j], r0, r1);
+      unpack_bf16x2(gu[j], g0, g1);
+      ou[j] = pack_bf16x2(r0 * inv * g0, r1 * inv * g1);
+    }
+    if (TWO_SHOT) {
+      for (int q = 0; q < a.world; ++q)
+        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[q] + a.off_normed) + row * a.H)[c] = o;
+    } else {
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[a.rank] + a.off_normed) + row * a.H)[c] = o;
+    }
+  }
+}
+
+// ROW_BLOCK: one 256-thread block per row (every 16-byte chunk of the row loaded at once; best when
+// a rank reduces few rows, e.g. decode); otherwise one warp per row (best for prefill-sized T).
+template <int MAXV, bool TWO_SHOT, bool ROW_BLOCK>
 __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   __shared__ float red[32];
   __shared__ int s_ok;
@@ -152,24 +262,50 @@ __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   const bool ok = block_barrier(a, 0, e, &s_ok);
   if (threadIdx.x == 0) a.epoch[b] = e;
   if (!ok) return;
-
-  float x[MAXV][8];
-  float inv;
-  if (!TWO_SHOT) {
-    for (long row = b; row < a.T; row += gridDim.x) {
-      reduce_norm_row<MAXV>(a, row, x, red, inv);
-      store_row<MAXV>(a, a.rank, row, x, inv);
-    }
-  } else {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long gw = (long)b * (AR_THREADS / 32) + warp;
+  const long nw = (long)gridDim.x * (AR_THREADS / 32);
+  long r0 = 0, r1 = a.T;
+  if (TWO_SHOT) {
     const int base_rows = a.T / a.world, extra = a.T % a.world;
-    const long r0 = (long)a.rank * base_rows + min(a.rank, extra);
-    const long r1 = r0 + base_rows + (a.rank < extra ? 1 : 0);
+    r0 = (long)a.rank * base_rows + min(a.rank, extra);
+    r1 = r0 + base_rows + (a.rank < extra ? 1 : 0);
+  }
+  if (ROW_BLOCK) {
+    float x[MAXV][8];
+    float inv;
     for (long row = r0 + b; row < r1; row += gridDim.x) {
       reduce_norm_row<MAXV>(a, row, x, red, inv);
-      for (int p = 0; p < a.world; ++p) store_row<MAXV>(a, (a.rank + p) % a.world, row, x, inv);
+      if (TWO_SHOT) {
+        for (int p = 0; p < a.world; ++p) store_row<MAXV>(a, (a.rank + p) % a.world, row, x, inv);
+      } else {
+        store_row<MAXV>(a, a.rank, row, x, inv);
+      }
     }
+  } else {
+    for (long row = r0 + gw; row < r1; row += nw) warp_reduce_norm_row<TWO_SHOT>(a, row, lane);
+  }
+  if (TWO_SHOT) {
     __threadfence_system();
     block_barrier(a, 1, e, &s_ok);
+  }
+}
+
+// Rows this rank reduces; block-per-row up to 255 rows, warp-per-row (8 rows per block) above.
+inline void launch_ar(const ArArgs& a, bool two_shot, cudaStream_t st) {
+  const long rows = two_shot ? (a.T + a.world - 1) / a.world : a.T;
+  const bool row_block = rows < AR_MAX_BLOCKS;
+  const int nb = row_block ? (int)std::max<long>(1, rows) : (int)std::min<long>((rows + 7) / 8, AR_MAX_BLOCKS - 1);
+  if (two_shot) {
+    if (row_block)
+      launch_k(ar_norm_kernel<4, true, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+    else
+      launch_k(ar_norm_kernel<4, true, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+  } else {
+    if (row_block)
+      launch_k(ar_norm_kernel<4, false, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+    else
+      launch_k(ar_norm_kernel<4, false, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
   }
 }
 
@@ -205,11 +341,7 @@ void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, i
   a.err = err.data_ptr<int>();
   a.timeout_ns = (uint64_t)(timeout_s * 1e9);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int nb = (int)nblocks;
-  if (two_shot)
-    launch_k(ar_norm_kernel<4, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
-  else
-    launch_k(ar_norm_kernel<4, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+  launch_ar(a, two_shot, st);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -246,5 +378,42 @@ void ar_barrier(const at::Tensor& bases, int64_t off_flags, int64_t rank, int64_
 }
 
 int64_t ar_flags_bytes() { return 2L * AR_MAX_BLOCKS * AR_MAX_RANKS * 4; }
+
+// Second half of the fused GEMM -> reduce-scatter: the o_proj / down GEMMs of all ranks already
+// pushed their partial rows into this rank's slots over NVLink (two-shot: only the rows this rank
+// owns; one-shot: every row). Wait for the peers, sum the slots from local memory, add the
+// residual, RMSNorm, and (two-shot) all-gather the resulting rows into every rank.
+void ar_push_reduce_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_push, int64_t off_resid,
+                         int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t t_max, int64_t H,
+                         const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
+                         bool two_shot, double timeout_s) {
+  TORCH_CHECK(world >= 1 && world <= AR_MAX_RANKS && bases.numel() == world && bases.device().is_cpu(),
+              "ar_push_reduce_norm: bases");
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * AR_THREADS * 4 && T <= t_max, "ar_push_reduce_norm: shapes");
+  TORCH_CHECK(nblocks >= 1 && nblocks < AR_MAX_BLOCKS, "ar_push_reduce_norm: nblocks");
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(gamma.device());
+  ArArgs a{};
+  auto bp = bases.data_ptr<int64_t>();
+  for (int i = 0; i < world; ++i) a.base[i] = (uint64_t)bp[i];
+  a.off_flags = off_flags;
+  a.off_resid = off_resid;
+  a.off_normed = off_normed;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.T = (int)T;
+  a.H = (int)H;
+  a.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr());
+  a.eps = (float)eps;
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.err = err.data_ptr<int>();
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.push = 1;
+  a.off_push = off_push;
+  a.t_max = (int)t_max;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  launch_ar(a, two_shot, st);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 }  // namespace mesh

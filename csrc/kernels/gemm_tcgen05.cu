@@ -56,8 +56,37 @@ struct GemmParams {
   int* err;
   uint32_t idesc;
   uint32_t tmem_cols;
-  unsigned long long* trace;  // optional [grid][8] %globaltimer stamps (nullptr: off)
+  unsigned long long* trace;  // optional [grid][16] %globaltimer stamps (nullptr: off)
+  // Fused reduce-scatter: instead of `out`, bf16 rows go to slot `my_rank` of the destination
+  // rank's symmetric buffer over NVLink (1: each token row to its owner rank, 2: to every rank).
+  int push_mode, my_rank, world, push_rows;
+  long slot_stride;                  // elements between source slots in a destination buffer
+  unsigned long long peer_base[8];   // destination buffer base (as mapped here) per rank
 };
+
+// owner rank of token row t when `rows` tokens are split into `world` near-equal ranges
+__device__ __forceinline__ int row_owner(int t, int rows, int world) {
+  const int base = rows / world, extra = rows % world;
+  const int big = extra * (base + 1);
+  if (t < big) return t / (base + 1);
+  return extra + (base > 0 ? (t - big) / base : 0);
+}
+
+// store two adjacent bf16 outputs of token row `tok`, feature `f` (f even)
+__device__ __forceinline__ void store_out2(const GemmParams& p, int tok, int f, uint32_t v) {
+  if (p.push_mode == 0) {
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (long)tok * p.ldo + f) = v;
+    return;
+  }
+  const long off = (long)p.my_rank * p.slot_stride + (long)tok * p.ldo + f;
+  if (p.push_mode == 1) {
+    const int d = row_owner(tok, p.push_rows, p.world);
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.peer_base[d]) + off) = v;
+  } else {
+    for (int d = 0; d < p.world; ++d)
+      *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.peer_base[d]) + off) = v;
+  }
+}
 
 struct Smem {
   uint8_t* a;
@@ -221,7 +250,7 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, uint32_t slo
         float a = S0((rp * 2), c);
         float b = (m + 1 < p.M) ? S0((rp * 2 + 1), c) : 0.f;
         if (m + 1 < p.M)
-          *reinterpret_cast<uint32_t*>(out + (long)n * p.ldo + m) = pack_bf16x2(a, b);
+          store_out2(p, n, m, pack_bf16x2(a, b));
         else
           out[(long)n * p.ldo + m] = f2bf(a);
       }
@@ -234,7 +263,7 @@ __device__ __forceinline__ void finalize_chunk(const GemmParams& p, uint32_t slo
         if (m >= p.M || n >= p.N) continue;
         float a = S0(r, cp), b = S0(r, cp + 1);
         if (n + 1 < p.N)
-          *reinterpret_cast<uint32_t*>(out + (long)m * p.ldo + n) = pack_bf16x2(a, b);
+          store_out2(p, m, n, pack_bf16x2(a, b));
         else
           out[(long)m * p.ldo + n] = f2bf(a);
       }
@@ -659,6 +688,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
 
+  if (p.push_mode != 0 && warp >= 2) __threadfence_system();  // pushed tiles visible to the peers
   if (trace && threadIdx.x == 64) trace[6] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
@@ -758,7 +788,7 @@ static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode) 
 // out = A @ B^T (normal) or out^T = A @ B^T (trans). Returns nothing; errors go to `err`.
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn_req,
                   int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
-                  const c10::optional<at::Tensor>& trace) {
+                  const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm_tcgen05: tensors must be CUDA");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_tcgen05: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tcgen05: A [M,K], B [N,K]");
@@ -802,6 +832,18 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   p.stages = stages;
   p.out = out.data_ptr();
   p.ldo = epi == EPI_ARGMAX ? out.size(1) : out.stride(0);
+  // push = [mode, my_rank, world, rows, slot_stride, ldo, base_0 .. base_{world-1}]
+  if (!push.empty()) {
+    TORCH_CHECK(epi == EPI_STORE_BF16 && push.size() >= 6, "fused reduce-scatter needs the bf16 epilogue");
+    p.push_mode = (int)push[0];
+    p.my_rank = (int)push[1];
+    p.world = (int)push[2];
+    p.push_rows = (int)push[3];
+    p.slot_stride = push[4];
+    p.ldo = push[5];
+    TORCH_CHECK(p.world >= 1 && p.world <= 8 && (int)push.size() == 6 + p.world, "push: peer table");
+    for (int i = 0; i < p.world; ++i) p.peer_base[i] = (unsigned long long)push[6 + i];
+  }
   if (trace.has_value()) {
     TORCH_CHECK(trace->numel() >= (int64_t)pl.grid * 16 && trace->scalar_type() == at::kLong, "gemm trace buffer");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());

@@ -81,6 +81,9 @@ class LlamaRunner:
         self.max_tokens = max_tokens
         self.symm = None
         self.use_fused_ar = self.world > 1 and ecfg.allreduce_impl != "nccl"
+        # "push": the o_proj / down GEMM epilogues scatter partial rows to their owner ranks over
+        # NVLink (fused GEMM -> reduce-scatter); otherwise GEMMs write locally and the AR kernel pulls
+        self.push_rs = self.use_fused_ar and ecfg.allreduce_impl in ("push", "push_oneshot")
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group)
@@ -98,10 +101,12 @@ class LlamaRunner:
 
     def _two_shot(self, T: int) -> bool:
         impl = self.ecfg.allreduce_impl
-        if impl == "oneshot":
+        if impl in ("oneshot", "push_oneshot"):
             return False
         if impl == "twoshot":
             return True
+        if self.push_rs:
+            return T >= self.world  # pushing to the owner moves each row once; all-gather follows
         return T * self.H * 2 * (self.world - 1) > (1 << 20)  # > ~1 MiB read per rank: two-shot
 
     def _reduce(self, part: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor, gamma: torch.Tensor,
@@ -111,11 +116,16 @@ class LlamaRunner:
         eps = self.cfg.rms_norm_eps
         if self.world == 1:
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
+        elif self.push_rs:
+            self.symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
         elif self.use_fused_ar:
             self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
         else:  # NCCL baseline
             dist.all_reduce(part, group=self.group)
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
+
+    def _push(self, T: int, parity: int):
+        return self.symm.push_args(T, parity, self._two_shot(T)) if self.push_rs else None
 
     def _part_buf(self, T: int, parity: int, scratch: dict) -> torch.Tensor:
         if self.use_fused_ar:
@@ -161,12 +171,12 @@ class LlamaRunner:
                 ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
                                  self.window)
             part = self._part_buf(T, parity, bufs)
-            ops.linear(attn, L.wo, out=part)
+            ops.linear(attn, L.wo, out=part, push=self._push(T, parity))
             self._reduce(part, resid, normed, L.mlp_norm, parity)
             parity ^= 1
             ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
             part = self._part_buf(T, parity, bufs)
-            ops.linear(h, L.wdown, out=part)
+            ops.linear(h, L.wdown, out=part, push=self._push(T, parity))
             gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
             self._reduce(part, resid, normed, gamma, parity)
             parity ^= 1

@@ -103,7 +103,7 @@ def scratch(device=None) -> DeviceScratch:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16, trans: bool = False,
-         bn: int = 0, mode: int = 0, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+         bn: int = 0, mode: int = 0, trace: Optional[torch.Tensor] = None, push: Optional[list] = None) -> torch.Tensor:
     """out = a @ b.T (trans=False, out [M, N']) or out^T = a @ b.T (trans=True, out [N, M'])
     with the tcgen05 kernel. a [M, K], b [N, K] bf16 K-contiguous. mode: 0 auto schedule,
     1 whole tiles only, 2 stream-K for the tail waves."""
@@ -121,7 +121,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STO
         bn_ = bn or ext().gemm_plan(M, N, K, epi, trans, a.device.index)[0]
         tiles = ((M + 127) // 128) * ((N + bn_ - 1) // bn_)
         s.ensure_gemm((tiles + s.num_sms) * 128 * bn_, tiles)
-    ext().gemm_tcgen05(a, b, out, epi, trans, bn, mode, s.gemm_ws, s.gemm_counters, s.err, trace)
+    ext().gemm_tcgen05(a, b, out, epi, trans, bn, mode, s.gemm_ws, s.gemm_counters, s.err, trace, push or [])
     _count()
     return out
 
@@ -130,7 +130,7 @@ _PLANS = {}
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, epi: int = EPI_STORE_BF16,
-           swap_ab: Optional[bool] = None) -> torch.Tensor:
+           swap_ab: Optional[bool] = None, push: Optional[list] = None) -> torch.Tensor:
     """y = x @ w.T for x [T, K], w [N, K] (nn.Linear layout). Decode-sized T uses swap-AB so the
     weight rows fill the 128-row MMA tile; large T uses the normal orientation."""
     T, N = x.shape[0], w.shape[0]
@@ -140,8 +140,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     if swap_ab is None:
         swap_ab = T <= SWAP_AB_MAX_TOKENS
     if swap_ab:
-        return gemm(w, x, out, epi, trans=True)
-    return gemm(x, w, out, epi, trans=False)
+        return gemm(w, x, out, epi, trans=True, push=push)
+    return gemm(x, w, out, epi, trans=False, push=push)
 
 
 def add_rmsnorm(resid: torch.Tensor, gamma: torch.Tensor, normed: torch.Tensor, eps: float,

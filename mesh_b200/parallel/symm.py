@@ -30,15 +30,18 @@ def _align(x: int, a: int = 256) -> int:
 class SymmLayout:
     t_max: int
     hidden: int
+    world: int
     off_flags: int
     off_p0: int
     off_p1: int
     off_resid: int
     off_normed: int
+    off_push0: int
+    off_push1: int
     total: int
 
     @classmethod
-    def make(cls, t_max: int, hidden: int, flags_bytes: int) -> "SymmLayout":
+    def make(cls, t_max: int, hidden: int, flags_bytes: int, world: int = 1) -> "SymmLayout":
         row = t_max * hidden * 2
         o = 0
         off_flags = o; o = _align(o + flags_bytes)
@@ -46,7 +49,10 @@ class SymmLayout:
         off_p1 = o; o = _align(o + row)
         off_resid = o; o = _align(o + row)
         off_normed = o; o = _align(o + row)
-        return cls(t_max, hidden, off_flags, off_p0, off_p1, off_resid, off_normed, o)
+        # fused reduce-scatter targets: per parity, one [t_max, H] slot per source rank
+        off_push0 = o; o = _align(o + world * row)
+        off_push1 = o; o = _align(o + world * row)
+        return cls(t_max, hidden, world, off_flags, off_p0, off_p1, off_resid, off_normed, off_push0, off_push1, o)
 
 
 class SymmWorkspace:
@@ -58,7 +64,7 @@ class SymmWorkspace:
         self.group = group or dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
-        self.layout = SymmLayout.make(t_max, hidden, ops.ext().ar_flags_bytes())
+        self.layout = SymmLayout.make(t_max, hidden, ops.ext().ar_flags_bytes(), self.world)
         self.buf = symm_mem.empty(self.layout.total, dtype=torch.uint8, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
@@ -92,11 +98,33 @@ class SymmWorkspace:
             raise ValueError(f"T={T} exceeds symmetric workspace capacity {L.t_max}")
         if nblocks <= 0:
             rows = (T + self.world - 1) // self.world if two_shot else T
-            nblocks = max(1, min(rows, 128))
+            nblocks = max(1, min((rows + 7) // 8, 255))  # 8 warps per block, one row per warp
         s = ops.scratch(self.device)
         ops.ext().ar_fused_norm(self.bases, L.off_flags, L.off_p0, L.off_p1, L.off_resid, L.off_normed,
                                 self.rank, self.world, T, L.hidden, parity, gamma, eps, self.epoch, s.err,
                                 nblocks, two_shot, timeout_s)
+        ops._count()
+
+    def push_args(self, T: int, parity: int, two_shot: bool) -> list:
+        """GEMM epilogue push table: [mode, my_rank, world, rows, slot_stride, ldo, peer bases...]."""
+        L = self.layout
+        off = L.off_push0 if parity % 2 == 0 else L.off_push1
+        return [1 if two_shot else 2, self.rank, self.world, T, L.t_max * L.hidden, L.hidden] + \
+            [int(b) + off for b in self.bases.tolist()]
+
+    def push_reduce_norm(self, T: int, parity: int, gamma: torch.Tensor, eps: float, two_shot: bool,
+                         nblocks: int = 0, timeout_s: float = 5.0):
+        L = self.layout
+        if T > L.t_max:
+            raise ValueError(f"T={T} exceeds symmetric workspace capacity {L.t_max}")
+        if nblocks <= 0:
+            rows = (T + self.world - 1) // self.world if two_shot else T
+            nblocks = max(1, min((rows + 7) // 8, 255))
+        s = ops.scratch(self.device)
+        off = L.off_push0 if parity % 2 == 0 else L.off_push1
+        ops.ext().ar_push_reduce_norm(self.bases, L.off_flags, off, L.off_resid, L.off_normed, self.rank,
+                                      self.world, T, L.t_max, L.hidden, gamma, eps, self.epoch, s.err, nblocks,
+                                      two_shot, timeout_s)
         ops._count()
 
     def reset(self):

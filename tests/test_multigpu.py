@@ -92,6 +92,40 @@ def _ar_check(rank, world):
             parity ^= 1
 
 
+def _push_check(rank, world):
+    """Fused GEMM -> reduce-scatter: every rank's GEMM epilogue pushes its partial rows to the owner
+    ranks over NVLink, then the owners reduce locally, add the residual, normalise and all-gather."""
+    import torch.distributed as dist
+    from mesh_b200 import ops
+    from mesh_b200.ops import reference as ref
+    from mesh_b200.parallel.symm import SymmWorkspace
+    dev = torch.device("cuda", rank)
+    H, K = 2048, 1024
+    ws = SymmWorkspace(512, H, dev)
+    gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    w = (torch.randn(H, K, generator=torch.Generator().manual_seed(50 + rank)) * 0.05).to(torch.bfloat16).to(dev)
+    parity = 0
+    for T, two_shot in ((64, True), (1, False), (300, True), (5, False)):
+        x = torch.randn(T, K, generator=torch.Generator().manual_seed(T + 7 * rank)).to(torch.bfloat16).to(dev)
+        resid0 = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(torch.bfloat16).to(dev)
+        ws.resid(T).copy_(resid0)
+        ops.linear(x, w, out=torch.empty(T, H, dtype=torch.bfloat16, device=dev),
+                   push=ws.push_args(T, parity, two_shot))
+        ws.push_reduce_norm(T, parity, gamma, 1e-5, two_shot=two_shot)
+        torch.cuda.synchronize()
+        ops.scratch(dev).check("push")
+        part = (x.float() @ w.float().T).to(torch.bfloat16)
+        allp = torch.empty(world, T, H, dtype=torch.bfloat16, device=dev)
+        dist.all_gather_into_tensor(allp.view(-1), part.contiguous().view(-1))
+        want_r = (resid0.float() + allp.float().sum(0))
+        got = ws.resid(T).float()
+        e = ((got - want_r).norm() / want_r.norm()).item()
+        en = ((ws.normed(T).float() - ref.rmsnorm(want_r.to(torch.bfloat16).float(), gamma, 1e-5)).norm() /
+              want_r.norm()).item()
+        assert e < 2e-2 and en < 2e-2, (T, two_shot, e, en)
+        parity ^= 1
+
+
 def _timeout_check(rank, world):
     import time
     import torch.distributed as dist
@@ -170,6 +204,10 @@ def _need_gpus():
 
 def test_fused_allreduce_norm_2gpu():
     _run(_ar_check, 2)
+
+
+def test_fused_gemm_reduce_scatter_push_2gpu():
+    _run(_push_check, 2)
 
 
 def test_allreduce_bounded_wait_reports_timeout_2gpu():
