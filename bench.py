@@ -40,6 +40,7 @@ def parse():
     ap.add_argument("--prefill-chunk", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the metric)")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-nvls", action="store_true", help="fused all-reduce on plain peer loads, not NVSwitch multicast")
     ap.add_argument("--ar-impl", default="auto",
                     choices=["auto", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
                     help="TP all-reduce: peer-memory pull (one/two-shot), fused GEMM->reduce-scatter push, or NCCL")
@@ -131,7 +132,7 @@ def main():
     max_seq = (P + G + 15) // 16 * 16
     ecfg = EngineConfig(tp=world, max_seq_len=max_seq, prefill_chunk_tokens=args.prefill_chunk,
                         use_cuda_graphs=not args.no_graphs, max_decode_batch_size=S,
-                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl)
+                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl, nvls=not args.no_nvls)
     w = synthetic_device_weights(cfg, rank, world, seed=1234, device=dev)
     pages = S * (max_seq // 16) + 64
     kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
@@ -181,12 +182,16 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
     launches = ops.LAUNCHES[0] - l0
+    # diagnostic outside the timed region: device time of one full-batch decode step alone (graph
+    # replays back to back, no host work between them), to separate device time from host overhead
+    dec_graph_ms = _decode_device_ms(eng, S, dist if world > 1 else None)
     keys = ["total_ms", "prefill_ms", "decode_ms", "p50_ttft_ms"]
     local = torch.tensor([sum(r[k] for r in res) for k in keys[:3]] +
-                         [sorted(r["p50_ttft_ms"] for r in res)[len(res) // 2]], dtype=torch.float64, device=dev)
+                         [sorted(r["p50_ttft_ms"] for r in res)[len(res) // 2], dec_graph_ms],
+                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(local, op=dist.ReduceOp.MAX)
-    total_ms, prefill_ms, decode_ms, p50_ttft = local.tolist()
+    total_ms, prefill_ms, decode_ms, p50_ttft, dec_graph_ms = local.tolist()
     K = args.steps
     decode_tokens = S * (G - 1) * K
     value = decode_tokens / (decode_ms / 1e3)
@@ -201,6 +206,7 @@ def main():
             "impl": args.impl,
             "p50_ttft_ms": round(p50_ttft, 3), "prefill_ms_per_step": round(prefill_ms / K, 3),
             "decode_ms_per_step": round(decode_ms / K, 3),
+            "decode_step_device_ms": round(dec_graph_ms, 4),
             "prefill_tokens_per_s": round(S * P * K / (prefill_ms / 1e3), 1),
             "config": {"model": args.model + ("" if not args.layers else f"-L{args.layers}-INVALID"),
                        "global_batch": S, "seq_len": P, "gen_tokens": G, "kv_page_tokens": 16,
@@ -217,6 +223,24 @@ def main():
     eng.close()
     torch.cuda.synchronize()
     mdist.shutdown()
+
+
+def _decode_device_ms(eng, batch, dist, reps=20):
+    """Mean device time of one decode step at ``batch`` sessions with nothing between steps."""
+    d = eng.dec
+    b = d.bucket_for(batch)
+    for _ in range(3):
+        d.step(b)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        d.step(b)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
 
 
 if __name__ == "__main__":

@@ -28,7 +28,7 @@ void attn_prefill(const at::Tensor& q, const at::Tensor& kcache, const at::Tenso
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
                    const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
-                   bool two_shot, double timeout_s);
+                   bool two_shot, double timeout_s, int64_t mc_base, const at::Tensor& trace);
 void ar_barrier(const at::Tensor& bases, int64_t off_flags, int64_t rank, int64_t world, at::Tensor& epoch,
                 at::Tensor& err, double timeout_s, const at::Tensor& device_ref);
 int64_t ar_flags_bytes();

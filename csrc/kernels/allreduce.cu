@@ -48,6 +48,9 @@ struct ArArgs {
   int push;
   long off_push;
   int t_max;
+  // NVLS multicast base of the symmetric workspace (same offsets as base[]); 0 = plain peer loads
+  uint64_t mc;
+  uint64_t* trace;  // optional: block 0 records %globaltimer at start / after barrier / rows done / end
 };
 
 __device__ __forceinline__ uint32_t* flag_ptr(const ArArgs& a, int peer, int phase, int block, int src) {
@@ -69,12 +72,43 @@ __device__ __forceinline__ bool block_barrier(const ArArgs& a, int phase, uint32
 }
 
 // Reduce one row over `nsrc` partial sources, add residual, RMSNorm; returns values in x (fp32).
-template <int MAXV>
+__device__ __forceinline__ const uint4* src_row(const ArArgs& a, int p, long row) {
+  const __nv_bfloat16* s =
+      a.push ? reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_push) + ((long)p * a.t_max + row) * a.H
+             : reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H;
+  return reinterpret_cast<const uint4*>(s);
+}
+
+template <int MAXV, bool MC>
 __device__ __forceinline__ void reduce_norm_row(const ArArgs& a, long row, float (&x)[MAXV][8], float* red,
                                                 float& inv) {
   const int nvec = a.H / 8;
   const __nv_bfloat16* resid = reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_resid);
   float ss = 0.f;
+  // issue every source's loads before consuming any (one NVLink round trip per row, not one per
+  // rank); with NVLS the switch returns the sum over all ranks in a single load
+  constexpr int NSRC = MC ? 1 : AR_MAX_RANKS;
+  const int nsrc = MC ? 1 : a.world;
+  uint4 d[NSRC][MAXV];
+  if (MC) {
+    const uint4* sr = reinterpret_cast<const uint4*>(a.mc + a.off_partial[a.parity]) + row * nvec;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int v = threadIdx.x + i * AR_THREADS;
+      if (v < nvec) d[0][i] = multimem_ld_reduce_bf16x8(sr + v);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < NSRC; ++p) {
+    if (!MC && p < a.world) {
+      const uint4* sr = src_row(a, p, row);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int v = threadIdx.x + i * AR_THREADS;
+        if (v < nvec) d[p][i] = __ldcg(sr + v);
+      }
+    }
+  }
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * AR_THREADS;
@@ -83,19 +117,17 @@ __device__ __forceinline__ void reduce_norm_row(const ArArgs& a, long row, float
       const uint32_t* ru = reinterpret_cast<const uint32_t*>(&r);
 #pragma unroll
       for (int j = 0; j < 4; ++j) unpack_bf16x2(ru[j], x[i][2 * j], x[i][2 * j + 1]);
-      for (int p = 0; p < a.world; ++p) {
-        const __nv_bfloat16* src =
-            a.push ? reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_push) +
-                         ((long)p * a.t_max + row) * a.H + v * 8
-                   : reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H + v * 8;
-        uint4 d = __ldcg(reinterpret_cast<const uint4*>(src));
-        const uint32_t* du = reinterpret_cast<const uint32_t*>(&d);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float u0, u1;
-          unpack_bf16x2(du[j], u0, u1);
-          x[i][2 * j] += u0;
-          x[i][2 * j + 1] += u1;
+      for (int p = 0; p < NSRC; ++p) {
+        if (p < nsrc) {
+          const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[p][i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float u0, u1;
+            unpack_bf16x2(du[j], u0, u1);
+            x[i][2 * j] += u0;
+            x[i][2 * j + 1] += u1;
+          }
         }
       }
       // round the new residual to bf16 (what gets stored), normalise that value
@@ -119,12 +151,14 @@ __device__ __forceinline__ void reduce_norm_row(const ArArgs& a, long row, float
   __syncthreads();
 }
 
+// dst_rank < 0: multicast store into every rank (NVLS)
 template <int MAXV>
 __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long row, const float (&x)[MAXV][8],
                                           float inv) {
   const int nvec = a.H / 8;
-  __nv_bfloat16* resid = reinterpret_cast<__nv_bfloat16*>(a.base[dst_rank] + a.off_resid);
-  __nv_bfloat16* normed = reinterpret_cast<__nv_bfloat16*>(a.base[dst_rank] + a.off_normed);
+  const uint64_t db = dst_rank < 0 ? a.mc : a.base[dst_rank];
+  __nv_bfloat16* resid = reinterpret_cast<__nv_bfloat16*>(db + a.off_resid);
+  __nv_bfloat16* normed = reinterpret_cast<__nv_bfloat16*>(db + a.off_normed);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * AR_THREADS;
@@ -141,8 +175,13 @@ __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long ro
         rou[j] = pack_bf16x2(x[i][2 * j], x[i][2 * j + 1]);
         nou[j] = pack_bf16x2(x[i][2 * j] * inv * g0, x[i][2 * j + 1] * inv * g1);
       }
-      *reinterpret_cast<uint4*>(resid + row * a.H + v * 8) = ro;
-      *reinterpret_cast<uint4*>(normed + row * a.H + v * 8) = no;
+      if (dst_rank < 0) {
+        multimem_st_16(resid + row * a.H + v * 8, ro);
+        multimem_st_16(normed + row * a.H + v * 8, no);
+      } else {
+        *reinterpret_cast<uint4*>(resid + row * a.H + v * 8) = ro;
+        *reinterpret_cast<uint4*>(normed + row * a.H + v * 8) = no;
+      }
     }
   }
 }
@@ -152,20 +191,13 @@ __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long ro
 // (locally, and into every rank for two-shot) and accumulates the sum of squares; pass 2 re-reads the
 // residual it just wrote and stores the normalised row. No block-wide synchronisation per row, so
 // thousands of rows are in flight and remote-load latency overlaps.
-__device__ __forceinline__ const uint4* src_row(const ArArgs& a, int p, long row) {
-  const __nv_bfloat16* s =
-      a.push ? reinterpret_cast<const __nv_bfloat16*>(a.base[a.rank] + a.off_push) + ((long)p * a.t_max + row) * a.H
-             : reinterpret_cast<const __nv_bfloat16*>(a.base[p] + a.off_partial[a.parity]) + row * a.H;
-  return reinterpret_cast<const uint4*>(s);
-}
-
-template <bool TWO_SHOT>
+template <bool TWO_SHOT, bool MC>
 __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, int lane) {
   const int nvec = a.H / 8;
   uint4* resid_l = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[a.rank] + a.off_resid) + row * a.H);
   const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
   float ss = 0.f;
-  constexpr int U = 2;
+  constexpr int U = 4;
   for (int c0 = lane; c0 < nvec; c0 += 32 * U) {
     float acc[U][8];
     bool ok[U];
@@ -180,16 +212,31 @@ __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, 
         for (int j = 0; j < 4; ++j) unpack_bf16x2(ru[j], acc[u][2 * j], acc[u][2 * j + 1]);
       }
     }
-    for (int p = 0; p < a.world; ++p) {
-      const uint4* sr = src_row(a, p, row);
-      uint4 d[U];
+    constexpr int NSRC = MC ? 1 : AR_MAX_RANKS;
+    const int nsrc = MC ? 1 : a.world;
+    uint4 d[NSRC][U];
+    if (MC) {
+      const uint4* sr = reinterpret_cast<const uint4*>(a.mc + a.off_partial[a.parity]) + row * nvec;
 #pragma unroll
       for (int u = 0; u < U; ++u)
-        if (ok[u]) d[u] = __ldcg(sr + c0 + u * 32);
+        if (ok[u]) d[0][u] = multimem_ld_reduce_bf16x8(sr + c0 + u * 32);
+    }
+#pragma unroll
+    for (int p = 0; p < NSRC; ++p) {
+      if (!MC && p < a.world) {
+        const uint4* sr = src_row(a, p, row);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (ok[u]) d[p][u] = __ldcg(sr + c0 + u * 32);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < NSRC; ++p) {
+      if (p >= nsrc) continue;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         if (!ok[u]) continue;
-        const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[u]);
+        const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[p][u]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float x0, x1;
@@ -212,7 +259,10 @@ __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, 
         ss += r0 * r0 + r1 * r1;
       }
       const int c = c0 + u * 32;
-      if (TWO_SHOT) {
+      if (TWO_SHOT && MC) {
+        multimem_st_16(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.mc + a.off_resid) + row * a.H) + c, o);
+        resid_l[c] = o;  // the pass below re-reads it locally before the multicast lands
+      } else if (TWO_SHOT) {
         for (int q = 0; q < a.world; ++q)
           reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[q] + a.off_resid) + row * a.H)[c] = o;
       } else {
@@ -237,7 +287,9 @@ __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, 
       unpack_bf16x2(gu[j], g0, g1);
       ou[j] = pack_bf16x2(r0 * inv * g0, r1 * inv * g1);
     }
-    if (TWO_SHOT) {
+    if (TWO_SHOT && MC) {
+      multimem_st_16(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.mc + a.off_normed) + row * a.H) + c, o);
+    } else if (TWO_SHOT) {
       for (int q = 0; q < a.world; ++q)
         reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[q] + a.off_normed) + row * a.H)[c] = o;
     } else {
@@ -248,20 +300,27 @@ __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, 
 
 // ROW_BLOCK: one 256-thread block per row (every 16-byte chunk of the row loaded at once; best when
 // a rank reduces few rows, e.g. decode); otherwise one warp per row (best for prefill-sized T).
-template <int MAXV, bool TWO_SHOT, bool ROW_BLOCK>
+// MC: partial sums come from NVLS multicast loads (the switch adds the ranks' rows) and two-shot
+// results leave through multicast stores; otherwise plain peer loads / stores.
+template <int MAXV, bool TWO_SHOT, bool ROW_BLOCK, bool MC>
 __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   __shared__ float red[32];
   __shared__ int s_ok;
   __shared__ uint32_t s_epoch;
   const int b = blockIdx.x;
+  const bool tr = a.trace != nullptr && b == 0 && threadIdx.x == 0;
   griddep_wait();  // partials come from the GEMM just before
   griddep_launch_dependents();
+  if (tr) a.trace[0] = globaltimer_ns();
   if (threadIdx.x == 0) s_epoch = a.epoch[b] + 1;
   __syncthreads();
   const uint32_t e = s_epoch;
+  if (MC) fence_proxy_alias();  // partials were written through the unicast alias
   const bool ok = block_barrier(a, 0, e, &s_ok);
   if (threadIdx.x == 0) a.epoch[b] = e;
   if (!ok) return;
+  if (MC) fence_proxy_alias();
+  if (tr) a.trace[1] = globaltimer_ns();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long gw = (long)b * (AR_THREADS / 32) + warp;
   const long nw = (long)gridDim.x * (AR_THREADS / 32);
@@ -275,46 +334,64 @@ __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
     float x[MAXV][8];
     float inv;
     for (long row = r0 + b; row < r1; row += gridDim.x) {
-      reduce_norm_row<MAXV>(a, row, x, red, inv);
-      if (TWO_SHOT) {
+      reduce_norm_row<MAXV, MC>(a, row, x, red, inv);
+      if (TWO_SHOT && MC) {
+        store_row<MAXV>(a, -1, row, x, inv);
+      } else if (TWO_SHOT) {
         for (int p = 0; p < a.world; ++p) store_row<MAXV>(a, (a.rank + p) % a.world, row, x, inv);
       } else {
         store_row<MAXV>(a, a.rank, row, x, inv);
       }
     }
   } else {
-    for (long row = r0 + gw; row < r1; row += nw) warp_reduce_norm_row<TWO_SHOT>(a, row, lane);
+    for (long row = r0 + gw; row < r1; row += nw) warp_reduce_norm_row<TWO_SHOT, MC>(a, row, lane);
   }
+  if (tr) a.trace[2] = globaltimer_ns();
   if (TWO_SHOT) {
+    if (MC) fence_proxy_alias();
     __threadfence_system();
     block_barrier(a, 1, e, &s_ok);
+    if (MC) fence_proxy_alias();  // readers use the unicast alias of what arrived by multicast
   }
+  if (tr) a.trace[3] = globaltimer_ns();
 }
 
 // Rows this rank reduces; block-per-row up to 255 rows, warp-per-row (8 rows per block) above.
-inline void launch_ar(const ArArgs& a, bool two_shot, cudaStream_t st) {
+template <bool MC>
+inline void launch_ar_t(const ArArgs& a, bool two_shot, cudaStream_t st) {
   const long rows = two_shot ? (a.T + a.world - 1) / a.world : a.T;
   const bool row_block = rows < AR_MAX_BLOCKS;
   const int nb = row_block ? (int)std::max<long>(1, rows) : (int)std::min<long>((rows + 7) / 8, AR_MAX_BLOCKS - 1);
   if (two_shot) {
     if (row_block)
-      launch_k(ar_norm_kernel<4, true, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+      launch_k(ar_norm_kernel<4, true, true, MC>, dim3(nb), dim3(AR_THREADS), 0, st, a);
     else
-      launch_k(ar_norm_kernel<4, true, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+      launch_k(ar_norm_kernel<4, true, false, MC>, dim3(nb), dim3(AR_THREADS), 0, st, a);
   } else {
     if (row_block)
-      launch_k(ar_norm_kernel<4, false, true>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+      launch_k(ar_norm_kernel<4, false, true, MC>, dim3(nb), dim3(AR_THREADS), 0, st, a);
     else
-      launch_k(ar_norm_kernel<4, false, false>, dim3(nb), dim3(AR_THREADS), 0, st, a);
+      launch_k(ar_norm_kernel<4, false, false, MC>, dim3(nb), dim3(AR_THREADS), 0, st, a);
   }
+}
+
+inline void launch_ar(const ArArgs& a, bool two_shot, cudaStream_t st) {
+  if (a.mc != 0 && !a.push)
+    launch_ar_t<true>(a, two_shot, st);
+  else
+    launch_ar_t<false>(a, two_shot, st);
 }
 
 // One rank's view of the symmetric workspace and where its regions sit.
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
                    const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
-                   bool two_shot, double timeout_s) {
+                   bool two_shot, double timeout_s, int64_t mc_base, const at::Tensor& trace) {
   TORCH_CHECK(world >= 1 && world <= AR_MAX_RANKS, "ar_fused_norm: world size 1..8");
+  TORCH_CHECK(mc_base % 16 == 0, "ar_fused_norm: multicast base must be 16-byte aligned");
+  TORCH_CHECK(!trace.defined() || trace.numel() == 0 || (trace.is_cuda() && trace.numel() >= 4 &&
+                                                         trace.scalar_type() == at::kLong),
+              "ar_fused_norm: trace must be a CUDA int64 tensor of >= 4 elements");
   TORCH_CHECK(bases.numel() == world && bases.scalar_type() == at::kLong && bases.device().is_cpu(),
               "ar_fused_norm: bases must be a CPU int64 tensor of peer addresses");
   TORCH_CHECK(H % 8 == 0 && H <= 8 * AR_THREADS * 4, "ar_fused_norm: H % 8 and H <= 8192");
@@ -340,6 +417,8 @@ void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, i
   a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
   a.err = err.data_ptr<int>();
   a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.mc = (uint64_t)mc_base;
+  a.trace = (trace.defined() && trace.numel() > 0) ? reinterpret_cast<uint64_t*>(trace.data_ptr<int64_t>()) : nullptr;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   launch_ar(a, two_shot, st);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

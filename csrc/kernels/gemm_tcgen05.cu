@@ -10,10 +10,14 @@
 //  * normal (TRANS=false): out[m][n]; used for prefill (A = activations, B = weights);
 //  * swap-AB (TRANS=true): out[n][m]; used for decode (A = weights so the 128-row MMA M dimension
 //    runs over output features and the few decode tokens form a narrow N = BN tile).
-// Scheduling: whole tiles round-robin over a persistent grid, plus stream-K for the tail waves
-// (and for decode shapes with fewer tiles than SMs): k-iterations are split evenly over the CTAs;
-// contributors to a tile publish fp32 partials and the tile's owner CTA (the one holding its
-// first k-block) adds them to its own TMEM accumulator in a fixed order.
+// Scheduling: whole tiles round-robin over a persistent grid, plus stream-K for the tail waves:
+// k-iterations are split evenly over the CTAs; contributors to a tile publish fp32 partials and
+// the tile's owner CTA (the one holding its first k-block) adds them to its own TMEM accumulator
+// in a fixed order. Swap-AB problems with fewer tiles than SMs (decode, and every tensor-parallel
+// shard of it) use cluster split-K instead: a thread-block cluster of C CTAs shares one output
+// tile, each CTA accumulates 1/C of the k-range in its own TMEM, stages it in its shared memory,
+// and after one cluster barrier every CTA sums its slice of the tile's columns over the C CTAs
+// through distributed shared memory (fixed order, deterministic) and runs the epilogue on it.
 //
 // Epilogues: bf16 store, f32 store, and SiLU(gate)*up for gate/up weights interleaved in blocks
 // of 64 features (rows g0..63,u0..63,g64..127,...), which writes half as many features.
@@ -24,6 +28,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -49,6 +55,10 @@ struct GemmParams {
   int dp_tiles;       // tiles [0, dp_tiles) are owned whole, round-robin over the grid
   int sk_iters_per_cta;  // stream-K share of the remaining tiles' k-iterations (0: none)
   int bn, stages;
+  int ck;             // cluster split-K: CTAs per cluster sharing one tile (<= 1: off)
+  int epi_bytes;      // shared memory of the epilogue region (staging, or split-K receive buffers)
+  int vec_out;        // output rows start 16-byte aligned: whole-tile epilogue may store 16 bytes at once
+  int direct_epi;     // whole tiles go TMEM -> registers -> global (else staged through shared memory)
   void* out;
   long ldo;
   float* workspace;   // stream-K partial tiles: slot (sk_tile + cta) x [BM][bn] fp32
@@ -112,7 +122,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
   s.b = ptr;
   ptr += (size_t)p.stages * p.bn * BK * 2;
   s.epi = reinterpret_cast<float*>(ptr);
-  ptr += 2 * EPI_SLOT_FLOATS * sizeof(float);
+  ptr += p.epi_bytes;
   ptr = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ptr) + 7) & ~uintptr_t(7));
   s.full = reinterpret_cast<uint64_t*>(ptr);
   s.empty = s.full + p.stages;
@@ -125,10 +135,17 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
   return s;
 }
 
-__host__ __device__ inline size_t gemm_smem_bytes(int stages, int bn) {
-  return 1024 + (size_t)stages * (A_STAGE_BYTES + bn * BK * 2) + 2 * EPI_SLOT_FLOATS * sizeof(float) + 8 +
+constexpr int EPI_STAGING_BYTES = 2 * EPI_SLOT_FLOATS * (int)sizeof(float);
+constexpr size_t SMEM_BUDGET = 232448;
+
+__host__ __device__ inline size_t gemm_smem_bytes(int stages, int bn, int epi_bytes = EPI_STAGING_BYTES) {
+  return 1024 + (size_t)stages * (A_STAGE_BYTES + bn * BK * 2) + (size_t)epi_bytes + 8 +
          (size_t)(2 * stages + 5) * 8 + 16;
 }
+
+// columns of the tile each CTA of a C-way cluster split owns, and its receive buffers' size
+__host__ __device__ inline int ck_cols(int bn, int C) { return ((bn + C - 1) / C + 3) & ~3; }
+__host__ __device__ inline int ck_recv_bytes(int bn, int C) { return C * BM * (ck_cols(bn, C) + 4) * 4; }
 
 // A segment is a contiguous k-range of one output tile processed by one CTA. Data-parallel
 // tiles are single segments; stream-K tiles are split across the CTAs whose k-iteration ranges
@@ -163,6 +180,22 @@ struct SegIter {
     if (p.sk_iters_per_cta == 0) g_end = g;
   }
   __device__ bool next(const GemmParams& p, Seg& s) {
+    if (p.ck > 1) {
+      // cluster split-K: one segment per CTA, k-range share `rank` of the cluster's tile
+      if (i > 0) return false;
+      ++i;
+      const int C = p.ck;
+      const int rank = (int)(blockIdx.x % C);
+      s.tile = (int)(blockIdx.x / C);
+      tile_coords(s.tile, p, s.tm, s.tn);
+      s.kb0 = (int)((long)rank * p.k_blocks / C);
+      s.kb1 = (int)((long)(rank + 1) * p.k_blocks / C);
+      s.sk_tile = -1;
+      s.contrib = rank;
+      s.ncontrib = C;
+      s.first_cta = 0;
+      return true;
+    }
     const int t_dp = blockIdx.x + i * gridDim.x;
     if (t_dp < p.dp_tiles) {
       ++i;
@@ -361,6 +394,351 @@ __device__ __forceinline__ void tmem_chunk_to_smem(uint32_t taddr_row, int col, 
   }
 }
 
+// ----------------------------------------------------------------------------------------------
+// cluster split-K epilogue (swap-AB orientation only). Every CTA of the cluster holds a partial
+// accumulator of the same 128 x bn tile for its share of the k-range. The tile's columns are
+// dealt out to the CTAs (CTA k owns columns [k * cpc, k * cpc + cpc), cpc = bn / C rounded up to
+// 4). Each thread reads its accumulator row out of TMEM and stores every column group straight
+// into the owning CTA's receive buffer through distributed shared memory (remote stores are
+// posted, nothing waits on a round trip): owner k's buffer is [C sources][128 rows][cpc + 4]
+// fp32 in its epilogue region, which nothing else uses in this mode (the operand ring may still
+// be busy in a slower peer). Every thread arrived on the cluster barrier at kernel start and
+// waits on it before its first remote store, so no CTA writes into a peer that has not started.
+// A second cluster barrier (release/acquire) makes the stores visible; then every CTA sums its
+// columns over the C sources in source order (deterministic) from local shared memory and runs
+// the epilogue. Both barriers are reached on every path, errors included.
+// ----------------------------------------------------------------------------------------------
+// ----------------------------------------------------------------------------------------------
+// Whole-tile epilogue straight from TMEM to global memory (no shared-memory staging): each thread
+// owns one accumulator row (TMEM lane). Swap-AB: the row is an output feature and its columns are
+// tokens, so for every token the 32 lanes of a warp write 32 consecutive features (64 B bf16).
+// Normal orientation: the row is a token and its 16-column chunks are 32 contiguous bytes, written
+// as 16-byte vectors. SiLU in swap-AB pairs gate row r with up row r + 64, which lives in another
+// warp: the up warps hand their chunk over in shared memory (double-buffered). The greedy-head
+// epilogue reduces (max, first index) per token over the 128 rows with warp shuffles and a
+// 4-entry cross-warp step. The TMEM buffer is released right after its last column is read.
+// ----------------------------------------------------------------------------------------------
+template <int EPI, bool TRANS>
+__device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem& s, uint32_t taddr_row, int row,
+                                                int lane, int quarter, int tm, int tn, uint64_t* tempty) {
+  const int m_base = tm * BM;
+  const int nchunks = (p.bn + 15) / 16;
+  float* xbuf = s.epi;  // SiLU hand-over [2][64][17] / argmax partials [2][4][16] x (value, index)
+  int chunk_i = 0;
+  auto release_if_last = [&](int c) {
+    if (c + 16 >= p.bn) {
+      tc_fence_before();
+      mbar_arrive(tempty);
+    }
+  };
+  if constexpr (EPI == EPI_SILU_BF16 && !TRANS) {
+    // gate columns g*128 + [0, 64), up columns g*128 + 64 + [0, 64); output column tn*bn/2 + g*64 + j
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    const int m = m_base + row;
+    for (int c = 0; c < p.bn / 2; c += 16) {
+      const int g = c / 64, j0 = c % 64;
+      uint32_t rg[16], ru[16];
+      tmem_ld16(taddr_row + g * 128 + j0, rg);
+      tmem_ld16(taddr_row + g * 128 + 64 + j0, ru);
+      tmem_ld_wait();
+      if (c + 16 >= p.bn / 2) {
+        tc_fence_before();
+        mbar_arrive(tempty);
+      }
+      const int n0 = tn * (p.bn / 2) + c;
+      if (m >= p.M) continue;
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        pk[i] = pack_bf16x2(silu_f(__uint_as_float(rg[2 * i])) * __uint_as_float(ru[2 * i]),
+                            silu_f(__uint_as_float(rg[2 * i + 1])) * __uint_as_float(ru[2 * i + 1]));
+      __nv_bfloat16* dst = out + (long)m * p.ldo + n0;
+      if (p.vec_out && n0 + 16 <= p.N / 2) {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+        for (int i = 0; i < 16 && n0 + i < p.N / 2; ++i)
+          dst[i] = f2bf(silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]));
+      }
+    }
+  } else if constexpr (EPI == EPI_SILU_BF16 && TRANS) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    const bool up = row >= 64;
+    const int q = row & 63;
+    const int m_out = tm * (BM / 2) + q;
+    for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
+      uint32_t r[16];
+      tmem_ld16(taddr_row + c, r);
+      tmem_ld_wait();
+      release_if_last(c);
+      float* xb = xbuf + (chunk_i & 1) * (64 * 17) + q * 17;
+      if (up) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xb[j] = __uint_as_float(r[j]);
+      }
+      named_bar_sync(1, 128);
+      if (!up && m_out < p.M / 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = tn * p.bn + c + j;
+          if (n < p.N) out[(long)n * p.ldo + m_out] = f2bf(silu_f(__uint_as_float(r[j])) * xb[j]);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    static_assert(TRANS, "argmax epilogue runs in swap-AB orientation");
+    const int m = m_base + row;
+    for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
+      uint32_t r[16];
+      tmem_ld16(taddr_row + c, r);
+      tmem_ld_wait();
+      release_if_last(c);
+      float* rv = xbuf + (chunk_i & 1) * 128;  // [4 quarters][16 tokens] values, then indices
+      int* ri = reinterpret_cast<int*>(rv + 64);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float best = (m < p.M) ? __uint_as_float(r[j]) : -INFINITY;
+        int bi = (m < p.M) ? m : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          rv[quarter * 16 + j] = best;
+          ri[quarter * 16 + j] = bi;
+        }
+      }
+      named_bar_sync(1, 128);
+      const int et = (threadIdx.x - 64);
+      if (et < 16) {
+        float best = rv[et];
+        int bi = ri[et];
+        for (int w = 1; w < 4; ++w) {
+          const float ov = rv[w * 16 + et];
+          const int oi = ri[w * 16 + et];
+          if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+          }
+        }
+        const int n = tn * p.bn + c + et;
+        if (n < p.N) reinterpret_cast<float2*>(p.out)[(long)tm * p.ldo + n] = make_float2(best, __int_as_float(bi));
+      }
+    }
+  } else if constexpr (TRANS) {
+    const int m = m_base + row;
+    for (int c = 0; c < p.bn; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(taddr_row + c, r);
+      tmem_ld_wait();
+      release_if_last(c);
+      if (m >= p.M) continue;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = tn * p.bn + c + j;
+        if (n >= p.N) break;
+        if constexpr (EPI == EPI_STORE_F32)
+          reinterpret_cast<float*>(p.out)[(long)n * p.ldo + m] = __uint_as_float(r[j]);
+        else
+          reinterpret_cast<__nv_bfloat16*>(p.out)[(long)n * p.ldo + m] = f2bf(__uint_as_float(r[j]));
+      }
+    }
+  } else {
+    const int m = m_base + row;
+    for (int c = 0; c < p.bn; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(taddr_row + c, r);
+      tmem_ld_wait();
+      release_if_last(c);
+      const int n0 = tn * p.bn + c;
+      if (m >= p.M) continue;
+      if constexpr (EPI == EPI_STORE_F32) {
+        float* dst = reinterpret_cast<float*>(p.out) + (long)m * p.ldo + n0;
+        if (p.vec_out && n0 + 16 <= p.N) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(dst)[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+        } else {
+          for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = __uint_as_float(r[i]);
+        }
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (long)m * p.ldo + n0;
+        if (p.vec_out && n0 + 16 <= p.N) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+          for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = f2bf(__uint_as_float(r[i]));
+        }
+      }
+    }
+  }
+}
+
+template <int EPI, bool TRANS>
+__device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, uint32_t tmem_base,
+                                            volatile int* abort_flag, unsigned long long* trace) {
+  static_assert(TRANS, "cluster split-K runs in swap-AB orientation");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int et = threadIdx.x - 64;      // 0..127
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;  // TMEM lane this thread may read
+  const int C = p.ck;
+  const uint32_t rank = cluster_ctarank();
+  int tm, tn;
+  tile_coords((int)(blockIdx.x / C), p, tm, tn);
+  const int cpc = ck_cols(p.bn, C);
+  const int ldr = cpc + 4;  // padded row stride of a receive slot (floats)
+  const uint32_t recv = smem_u32(s.epi);
+  const uint32_t slot_bytes = (uint32_t)(BM * ldr) * 4;
+
+  if (et == 0)
+    *s.epi_flag = mbar_wait_bounded(&s.tfull[0], 0, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag, WAIT_LIMIT_NS);
+  named_bar_sync(1, 128);
+  const int ok = *s.epi_flag;
+  tc_fence_after();
+  if (trace && et == 0) trace[5] = globaltimer_ns();
+  const uint32_t taddr_row = tmem_base + ((uint32_t)(quarter * 32) << 16);
+  // this CTA's slot in any owner's buffer, at this thread's row
+  const uint32_t my_slot_row = recv + rank * slot_bytes + (uint32_t)(row * ldr) * 4;
+  cluster_wait_acquire();  // pairs with the arrive at kernel start: every peer CTA is running
+  for (int c = 0; c < p.bn; c += 16) {
+    uint32_t r[16];
+    if (ok) {
+      tmem_ld16(taddr_row + c, r);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) r[i] = 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const int col = c + i;
+      const int owner = col / cpc;
+      const uint32_t local = my_slot_row + (uint32_t)(col - owner * cpc) * 4;
+      st_dsmem_f4(mapa_shared(local, (uint32_t)owner), __uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                  __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // every partial slice has landed in its owner's buffer
+  if (trace && et == 0) trace[8] = globaltimer_ns();
+
+  const int c_lo = (int)rank * cpc;
+  const int c_hi = min(p.bn, c_lo + cpc);
+  // v[j] = sum over the C sources of row r, owned columns c + 4j .. c + 4j + 3 (j < nv <= 8)
+  auto sum_row = [&](int r, int c, int nv, float4 (&v)[8]) {
+    const uint32_t off = (uint32_t)(r * ldr + (c - c_lo)) * 4;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < C; ++k) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < nv) {
+          const float4 y = lds_f4(recv + (uint32_t)k * slot_bytes + off + 16u * j);
+          v[j].x += y.x; v[j].y += y.y; v[j].z += y.z; v[j].w += y.w;
+        }
+    }
+  };
+  const int m_base = tm * BM;
+  if constexpr (EPI == EPI_SILU_BF16) {
+    // rows 0..63 gate, 64..127 up; the two thread halves take alternate 16-column groups
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    const int q = et & 63, half = et >> 6;
+    const int m_out = tm * (BM / 2) + q;
+    for (int c = c_lo + 16 * half; c < c_hi; c += 32) {
+      const int nv = min(4, (c_hi - c) >> 2);
+      float4 g[8], u[8];
+      sum_row(q, c, nv, g);
+      sum_row(q + 64, c, nv, u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j >= nv) break;
+        const float gv[4] = {g[j].x, g[j].y, g[j].z, g[j].w}, uv[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = tn * p.bn + c + 4 * j + e;
+          if (n < p.N && m_out < p.M / 2) out[(long)n * p.ldo + m_out] = f2bf(silu_f(gv[e]) * uv[e]);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    // per token column: max over the tile's 128 rows (first index on ties) -> float2 [m_tiles][ldo]
+    float* red_v = reinterpret_cast<float*>(s.a);  // operand ring: idle once this CTA's MMAs completed
+    int* red_i = reinterpret_cast<int*>(s.a + 16 * 4);
+    const int m = m_base + et;
+    for (int c = c_lo; c < c_hi; c += 4) {
+      float4 v8[8];
+      sum_row(et, c, 1, v8);
+      const float vv[4] = {v8[0].x, v8[0].y, v8[0].z, v8[0].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float best = (m < p.M) ? vv[j] : -INFINITY;
+        int bi = (m < p.M) ? m : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          red_v[(et >> 5) * 4 + j] = best;
+          red_i[(et >> 5) * 4 + j] = bi;
+        }
+      }
+      named_bar_sync(1, 128);
+      if (et < 4) {
+        float best = red_v[et];
+        int bi = red_i[et];
+        for (int w = 1; w < 4; ++w) {
+          const float ov = red_v[w * 4 + et];
+          const int oi = red_i[w * 4 + et];
+          if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+          }
+        }
+        const int n = tn * p.bn + c + et;
+        if (n < p.N) reinterpret_cast<float2*>(p.out)[(long)tm * p.ldo + n] = make_float2(best, __int_as_float(bi));
+      }
+      named_bar_sync(1, 128);
+    }
+  } else {
+    const int m = m_base + et;
+    for (int c = c_lo; c < c_hi; c += 32) {
+      const int nv = min(8, (c_hi - c) >> 2);
+      float4 v[8];
+      sum_row(et, c, nv, v);
+      if (trace && et == 0 && c == c_lo) trace[11] = globaltimer_after(v[0].x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= nv) break;
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = tn * p.bn + c + 4 * j + e;
+          if (n >= p.N || m >= p.M) continue;
+          if constexpr (EPI == EPI_STORE_F32)
+            reinterpret_cast<float*>(p.out)[(long)n * p.ldo + m] = vv[e];
+          else
+            reinterpret_cast<__nv_bfloat16*>(p.out)[(long)n * p.ldo + m] = f2bf(vv[e]);
+        }
+      }
+    }
+  }
+  if (trace && et == 0) trace[9] = globaltimer_ns();
+}
+
 template <int EPI, bool TRANS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -397,6 +775,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_base;
   volatile int* abort_flag = s.abort_flag;
+  if (TRANS && p.ck > 1) cluster_arrive_relaxed();  // waited on before any remote shared-memory access
   unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * 16 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer_ns();
   // the next kernel may start its prologue on SMs this grid frees up
@@ -461,6 +840,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    __syncwarp();
+    if (TRANS && p.ck > 1) {
+      cluster_wait_acquire();
+      cluster_sync();
+    }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
     int stage = 0;
@@ -517,6 +901,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ++it;
     }
     if (trace && lane == 0) trace[4] = globaltimer_ns();
+    __syncwarp();
+    if (TRANS && p.ck > 1) {
+      cluster_wait_acquire();
+      cluster_sync();
+    }
+  } else if (TRANS && p.ck > 1) {
+    // ------------------------ epilogue, cluster split-K (warps 2..5) ------------------------
+    griddep_wait();
+    if constexpr (TRANS) ck_epilogue<EPI, TRANS>(p, s, tmem_base, abort_flag, trace);
   } else {
     // ------------------------------- epilogue (warps 2..5) -------------------------------
     griddep_wait();  // output and workspace may still be in use by the previous grid
@@ -546,7 +939,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t taddr_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
 
-      if (sg.ncontrib == 1) {
+      if (sg.ncontrib == 1 && p.push_mode == 0 && p.direct_epi) {
+        direct_epilogue<EPI, TRANS>(p, s, taddr_row, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
+      } else if (sg.ncontrib == 1) {
         const int nsteps = ChunkPlan<EPI, TRANS>::steps(p.bn);
         for (int st = 0; st < nsteps; ++st) {
           int ca, cb, cw, cout;
@@ -719,17 +1114,112 @@ static uint32_t tmem_cols_for(int bn) {
 }
 
 template <int EPI, bool TRANS>
-static void launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, size_t smem,
-                         cudaStream_t stream) {
+static void configure_kernel() {
   auto kern = gemm_tcgen05_kernel<EPI, TRANS>;
   static bool configured[64] = {false};
   int dev;
   cudaGetDevice(&dev);
   if (!configured[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured[dev] = true;
   }
-  launch_k(kern, dim3(grid), dim3(NUM_THREADS), smem, stream, ta, tb, p);
+}
+
+template <int EPI, bool TRANS>
+static void launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, size_t smem,
+                         cudaStream_t stream) {
+  auto kern = gemm_tcgen05_kernel<EPI, TRANS>;
+  configure_kernel<EPI, TRANS>();
+  launch_kc(kern, dim3(grid), dim3(NUM_THREADS), smem, stream, p.ck > 1 ? p.ck : 1, ta, tb, p);
+}
+
+// Largest number of co-resident clusters of `C` CTAs of this kernel (every CTA of a cluster split
+// must be resident at once, and one wave is the point of the schedule).
+template <int EPI, bool TRANS>
+static int max_active_clusters(int C, size_t smem) {
+  static std::mutex mu;
+  static std::unordered_map<long, int> cache;
+  int dev;
+  cudaGetDevice(&dev);
+  const long key = ((long)dev << 40) | ((long)C << 32) | (long)smem;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  configure_kernel<EPI, TRANS>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C * 64);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tcgen05_kernel<EPI, TRANS>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+static int max_active_clusters_for(int epi, bool trans, int C, size_t smem) {
+  if (!trans) return 0;
+  switch (epi) {
+    case EPI_STORE_BF16: return max_active_clusters<EPI_STORE_BF16, true>(C, smem);
+    case EPI_STORE_F32: return max_active_clusters<EPI_STORE_F32, true>(C, smem);
+    case EPI_SILU_BF16: return max_active_clusters<EPI_SILU_BF16, true>(C, smem);
+    case EPI_ARGMAX: return max_active_clusters<EPI_ARGMAX, true>(C, smem);
+    default: return 0;
+  }
+}
+
+static bool ck_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESH_GEMM_CK");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Cluster split-K factor for a swap-AB problem with `tiles` output tiles and `kb` k-blocks: the
+// largest C (<= 16, <= kb, tiles * C <= SMs) whose clusters all fit on the GPU at once; 0 if none
+// of C >= 2 qualifies.
+// shared-memory plan of one CTA: operand stages and epilogue region (receive buffers when C > 1)
+struct SmemPlan {
+  int stages, epi_bytes;
+  size_t bytes;
+};
+static int max_stages() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESH_GEMM_STAGES");
+    v = e ? std::max(2, std::min(8, std::atoi(e))) : 8;
+  }
+  return v;
+}
+
+static SmemPlan smem_plan(int bn, int C) {
+  SmemPlan sp;
+  sp.epi_bytes = C > 1 ? std::max(EPI_STAGING_BYTES, ck_recv_bytes(bn, C)) : EPI_STAGING_BYTES;
+  sp.stages = max_stages();
+  while (sp.stages > 2 && gemm_smem_bytes(sp.stages, bn, sp.epi_bytes) > SMEM_BUDGET) --sp.stages;
+  sp.bytes = gemm_smem_bytes(sp.stages, bn, sp.epi_bytes);
+  return sp;
+}
+
+static int pick_ck(int tiles, int kb, int num_sms, int epi, int bn) {
+  int C = std::min(16, std::min(kb, num_sms / std::max(tiles, 1)));
+  for (; C >= 2; --C) {
+    const SmemPlan sp = smem_plan(bn, C);
+    if (sp.bytes <= SMEM_BUDGET && max_active_clusters_for(epi, true, C, sp.bytes) >= tiles) return C;
+  }
+  return 0;
 }
 
 // Choose BN for a problem: decode (swap-AB) uses the token count rounded to 16, prefill 256 (or
@@ -749,15 +1239,30 @@ int gemm_pick_bn(int N, int epi, bool trans) {
 struct Plan {
   int grid, dp_tiles, sk_iters, sk_tiles, tiles;
   size_t ws_floats;
+  int ck;
 };
 
-static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode) {
+// force_mode: 0 auto, 1 data-parallel, 2 stream-K, 3 cluster split-K (swap-AB only).
+static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode, int epi = 0, bool trans = false,
+                      bool push = false) {
   Plan pl{};
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + bn - 1) / bn;
   const int kb = (K + BK - 1) / BK;
   pl.tiles = m_tiles * n_tiles;
   const long total_iters = (long)pl.tiles * kb;
   int grid = num_sms;
+  if (trans && !push && (force_mode == 3 || (force_mode == 0 && ck_enabled() && pl.tiles < num_sms))) {
+    const int C = pick_ck(pl.tiles, kb, num_sms, epi, bn);
+    if (C >= 2) {
+      pl.ck = C;
+      pl.grid = pl.tiles * C;
+      pl.dp_tiles = 0;
+      pl.sk_iters = 0;
+      pl.sk_tiles = 0;
+      pl.ws_floats = 0;
+      return pl;
+    }
+  }
   if (force_mode == 1 || (force_mode == 0 && (pl.tiles % grid == 0 || pl.tiles >= 4 * grid))) {
     // pure data-parallel persistent schedule
     pl.grid = pl.tiles < grid ? pl.tiles : grid;
@@ -816,7 +1321,14 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   p.n_tiles = (N + bn - 1) / bn;
   p.k_blocks = (K + BK - 1) / BK;
   const int sms = num_sms_cached(dev);
-  Plan pl = make_plan(M, N, K, bn, sms, (int)mode);
+  Plan pl = make_plan(M, N, K, bn, sms, (int)mode, (int)epi, trans, !push.empty());
+  p.ck = pl.ck;
+  TORCH_CHECK(mode != 3 || pl.ck >= 2, "gemm_tcgen05: cluster split-K requested but not possible for this shape");
+  TORCH_CHECK(p.ck <= 1 || (trans && push.empty()), "gemm_tcgen05: cluster split-K needs swap-AB and no push");
+  const SmemPlan sp = smem_plan(bn, p.ck);
+  TORCH_CHECK(sp.bytes <= SMEM_BUDGET, "gemm_tcgen05: shared memory plan exceeds the budget");
+  const int stages = sp.stages;
+  p.epi_bytes = sp.epi_bytes;
   p.dp_tiles = pl.dp_tiles;
   p.sk_iters_per_cta = pl.sk_iters;
   if (pl.sk_tiles > 0) {
@@ -826,12 +1338,15 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
     p.workspace = workspace.data_ptr<float>();
     p.counters = counters.data_ptr<int>();
   }
-  const size_t budget = 232448;
-  int stages = 8;
-  while (stages > 2 && gemm_smem_bytes(stages, bn) > budget) --stages;
   p.stages = stages;
   p.out = out.data_ptr();
   p.ldo = epi == EPI_ARGMAX ? out.size(1) : out.stride(0);
+  p.vec_out = ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
+              ((p.ldo * (epi == EPI_STORE_F32 ? 4 : 2)) % 16 == 0);
+  // Swap-AB CTAs that stream many tiles (LM head) keep the staged epilogue, whose cooperative
+  // column-at-a-time stores measured faster there; latency-bound few-tile launches and the normal
+  // orientation store straight from registers.
+  p.direct_epi = (!trans || pl.tiles <= 2 * pl.grid) ? 1 : 0;
   // push = [mode, my_rank, world, rows, slot_stride, ldo, base_0 .. base_{world-1}]
   if (!push.empty()) {
     TORCH_CHECK(epi == EPI_STORE_BF16 && push.size() >= 6, "fused reduce-scatter needs the bf16 epilogue");
@@ -855,7 +1370,7 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   CUtensorMap ta = tma_map_2d_bf16(A.data_ptr(), K, M, A.stride(0), BK, BM);
   CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, bn);
   const int grid = pl.grid;
-  const size_t smem = gemm_smem_bytes(stages, bn);
+  const size_t smem = sp.bytes;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   switch (epi * 2 + (trans ? 1 : 0)) {
     case EPI_STORE_BF16 * 2 + 0: launch_typed<EPI_STORE_BF16, false>(ta, tb, p, grid, smem, stream); break;
@@ -870,13 +1385,14 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// [bn, mode-independent workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters]
+// [bn, workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters, cluster split]
+// (the plan of the automatic schedule without a push table)
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device) {
+  const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
   int bn = gemm_pick_bn((int)N, (int)epi, trans);
-  Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0);
-  int stages = 8;
-  while (stages > 2 && gemm_smem_bytes(stages, bn) > 232448) --stages;
-  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, stages, pl.grid, pl.dp_tiles, pl.sk_iters};
+  Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0, (int)epi, trans, false);
+  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, smem_plan(bn, pl.ck).stages, pl.grid, pl.dp_tiles, pl.sk_iters,
+          pl.ck};
 }
 
 }  // namespace mesh

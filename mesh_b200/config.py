@@ -144,7 +144,8 @@ class EngineConfig:
     decode_batch_buckets: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
     prefill_chunk_tokens: int = 16384
     use_fused_allreduce: bool = True
-    allreduce_impl: str = "auto"  # auto | oneshot | twoshot | nccl
+    allreduce_impl: str = "auto"  # auto | oneshot | twoshot | push | push_oneshot | nccl
+    nvls: bool = True  # fused all-reduce through NVSwitch multicast (multimem) when the node has it
     extra: dict = field(default_factory=dict)
 
     def bucket_for(self, batch: int) -> int:

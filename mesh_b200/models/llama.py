@@ -86,7 +86,7 @@ class LlamaRunner:
         self.push_rs = self.use_fused_ar and ecfg.allreduce_impl in ("push", "push_oneshot")
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
-            self.symm = SymmWorkspace(max_tokens, self.H, self.device, group)
+            self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
         self._cand_gather = None
         # keep fp32 logits (tests, sampling); the greedy decode path fuses argmax into the LM head
         self.keep_logits = False

@@ -106,7 +106,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STO
          bn: int = 0, mode: int = 0, trace: Optional[torch.Tensor] = None, push: Optional[list] = None) -> torch.Tensor:
     """out = a @ b.T (trans=False, out [M, N']) or out^T = a @ b.T (trans=True, out [N, M'])
     with the tcgen05 kernel. a [M, K], b [N, K] bf16 K-contiguous. mode: 0 auto schedule,
-    1 whole tiles only, 2 stream-K for the tail waves."""
+    1 whole tiles only, 2 stream-K for the tail waves, 3 cluster split-K (swap-AB only)."""
     s = scratch(a.device)
     M, N, K = a.shape[0], b.shape[0], a.shape[1]
     if mode == 0 and bn == 0:

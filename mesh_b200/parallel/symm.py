@@ -8,13 +8,16 @@ One allocation per rank, mapped into every peer of the TP group (CUDA VMM/IPC th
 
 The o_proj / down_proj GEMMs write their partial sums into a partial slot; the ``ar_fused_norm``
 kernel reads the peers' slots over NVLink, adds the residual, applies RMSNorm and writes
-``resid`` / ``normed`` (locally for one-shot, into every peer for two-shot). Only plain P2P loads
-and stores touch peer memory; no TMA (and no multicast TMA) ever reads a peer address.
+``resid`` / ``normed`` (locally for one-shot, into every peer for two-shot). Peer memory is touched
+by plain P2P loads and stores, or, when the allocation is bound to an NVLink multicast object
+(NVSwitch NVLS), by ``multimem`` loads that return the sum over all ranks and ``multimem`` stores
+that write every rank at once. No TMA (and no multicast TMA) ever reads a peer address.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
-from typing import List
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
@@ -58,7 +61,8 @@ class SymmLayout:
 class SymmWorkspace:
     """Owns the symmetric buffer of this rank plus the peer address table."""
 
-    def __init__(self, t_max: int, hidden: int, device: torch.device, group=None):
+    def __init__(self, t_max: int, hidden: int, device: torch.device, group=None,
+                 multicast: Optional[bool] = None):
         import torch.distributed._symmetric_memory as symm_mem
         self.device = device
         self.group = group or dist.group.WORLD
@@ -73,8 +77,26 @@ class SymmWorkspace:
         ptrs: List[int] = list(self.handle.buffer_ptrs)
         if len(ptrs) != self.world:
             raise RuntimeError(f"symmetric rendezvous returned {len(ptrs)} peers for world {self.world}")
+        # peer tables are allocation bases; the workspace must start there for the offsets to hold
+        delta = self.buf.data_ptr() - ptrs[self.rank]
+        if delta != 0:
+            raise RuntimeError(f"symmetric workspace is at offset {delta} inside its allocation")
         self.bases = torch.tensor(ptrs, dtype=torch.int64)
+        # NVLS multicast address of the same allocation (0: plain peer loads). MESH_NVLS=0 turns it off.
+        if multicast is None:
+            multicast = os.environ.get("MESH_NVLS", "1") != "0"
+        mc = 0
+        if multicast and self.world > 1:
+            try:
+                mc = int(self.handle.multicast_ptr)
+            except Exception:
+                mc = 0
+        # every rank must agree, or some would multicast into an allocation others read unicast
+        flag = torch.tensor([1 if mc else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        self.mc_base = mc if int(flag.item()) == 1 else 0
         self.epoch = torch.zeros(256, dtype=torch.int32, device=device)
+        self._no_trace = torch.empty(0, dtype=torch.int64, device=device)
         dist.barrier(self.group)
 
     def view(self, off: int, rows: int) -> torch.Tensor:
@@ -92,7 +114,11 @@ class SymmWorkspace:
         return self.view(self.layout.off_normed, rows)
 
     def fused_allreduce_norm(self, T: int, parity: int, gamma: torch.Tensor, eps: float, two_shot: bool,
-                             nblocks: int = 0, timeout_s: float = 5.0):
+                             nblocks: int = 0, timeout_s: float = 5.0, multicast: bool = True,
+                             trace: Optional[torch.Tensor] = None):
+        """``multicast`` uses NVLS loads/stores when the workspace has them; ``trace`` (CUDA int64,
+        >= 4) receives block 0's %globaltimer at start, after the entry barrier, after the rows and
+        at the end."""
         L = self.layout
         if T > L.t_max:
             raise ValueError(f"T={T} exceeds symmetric workspace capacity {L.t_max}")
@@ -102,7 +128,8 @@ class SymmWorkspace:
         s = ops.scratch(self.device)
         ops.ext().ar_fused_norm(self.bases, L.off_flags, L.off_p0, L.off_p1, L.off_resid, L.off_normed,
                                 self.rank, self.world, T, L.hidden, parity, gamma, eps, self.epoch, s.err,
-                                nblocks, two_shot, timeout_s)
+                                nblocks, two_shot, timeout_s, self.mc_base if multicast else 0,
+                                self._no_trace if trace is None else trace)
         ops._count()
 
     def push_args(self, T: int, parity: int, two_shot: bool) -> list:

@@ -70,11 +70,14 @@ def bench_linear(name, T, N, K, epi, rows, hbm, tf):
     n_out = N // 2 if epi == ops.EPI_SILU_BF16 else N
     out = torch.empty(T, n_out, device=dev, dtype=torch.float32 if epi == ops.EPI_STORE_F32 else torch.bfloat16)
     us = timeit(lambda i: ops.linear(x, ws[i % nc], out=out, epi=epi))
+    # the same product through cuBLAS (plain bf16 output, no fused epilogue), for reference
+    ref_out = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+    us_cublas = timeit(lambda i: torch.mm(x, ws[i % nc].t(), out=ref_out))
     byts = w_bytes + T * K * 2 + out.numel() * out.element_size()
     flops = 2.0 * T * N * K
     rows.append(dict(op=name, shape=f"T={T} N={N} K={K}", us=round(us, 2), GBps=round(byts / us / 1e3, 1),
                      TFLOPs=round(flops / us / 1e6, 1), hbm_frac=round(byts / us / 1e3 / hbm, 3),
-                     tc_frac=round(flops / us / 1e6 / tf, 3)))
+                     tc_frac=round(flops / us / 1e6 / tf, 3), cublas_us=round(us_cublas, 2)))
     del ws
 
 
@@ -103,15 +106,17 @@ def trace_gemms(cfg, s, T, modes=(0, 1)):
             med = lambda c: round(float(rel[:, c].median()), 2)
             mx = lambda c: round(float(rel[:, c].max()), 2)
             contrib = rel[t[:, 8] > 0]
-            owner = rel[t[:, 10] > 0]
+            owner = rel[t[:, 12] > 0]
             cm = lambda x, c: round(float(x[:, c].median()), 2) if len(x) else None
-            print(json.dumps(dict(trace=name, mode=mode, ctas=len(t), start_max=mx(0), waited=med(1),
+            plan = ops.ext().gemm_plan(N, T, K, epi, True, torch.cuda.current_device())
+            print(json.dumps(dict(trace=name, mode=mode, plan=list(plan), ctas=len(t), start_max=mx(0), waited=med(1),
                                   first_data_med=med(3), mma_done_med=med(4), mma_done_max=mx(4),
                                   epi_done_max=mx(6), exit_max=mx(7), contrib_n=len(contrib),
                                   contrib_partial_written=cm(contrib, 8), contrib_flag_set=cm(contrib, 9),
                                   owner_n=len(owner), owner_wait_done=cm(owner, 10),
                                   owner_bulk_landed=cm(owner, 12), owner_add0=cm(owner, 13),
-                                  owner_fin0=cm(owner, 14), owner_done=cm(owner, 11))))
+                                  owner_fin0=cm(owner, 14), owner_done=cm(owner, 11),
+                                  ck_first_sum=med(11) if plan[7] > 1 else None)))
 
 
 def main():

@@ -100,6 +100,69 @@ def test_gemm_stream_k_matches_data_parallel(M, N, K, epi):
     assert torch.equal(o2, o3)  # deterministic
 
 
+@pytest.mark.parametrize("M,N,K", [(768, 64, 4096), (6144, 64, 4096), (4096, 17, 512), (3584, 64, 4096),
+                                   (300, 8, 1024), (128, 1, 128), (1024, 128, 2048)])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_cluster_split_k(M, N, K, epi):
+    """Cluster split-K (swap-AB: M weight rows, N tokens): every CTA of a cluster accumulates a
+    share of the k-range and the shares are summed through distributed shared memory."""
+    if epi == 2 and M % 128:
+        pytest.skip("SiLU epilogue needs the feature dim % 128")
+    w = _rand(M, K, std=0.05, seed=21)
+    x = _rand(N, K, seed=22)
+    want = x.float() @ w.float().T
+    if epi == 2:
+        want = ref.silu_mul_interleaved(want)
+    dt = torch.float32 if epi == 1 else torch.bfloat16
+    out = torch.empty(N, want.shape[1], dtype=dt, device=DEV)
+    ops.gemm(w, x, out, epi, trans=True, mode=3)
+    torch.cuda.synchronize()
+    assert rel_err(out, want) < (2e-3 if epi == 1 else 1e-2)
+    again = torch.empty_like(out)
+    ops.gemm(w, x, again, epi, trans=True, mode=3)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)  # fixed summation order
+
+
+@pytest.mark.parametrize("V,T", [(4096, 64), (16032, 64), (1000, 5)])
+def test_lm_head_argmax_cluster_split(V, T):
+    """Fused greedy head on shapes that take the cluster split-K schedule."""
+    H = 4096
+    w = _rand(V, H, std=0.05, seed=23)
+    x = _rand(T, H, seed=24)
+    logits = x.float() @ w.float().T
+    tiles = torch.empty((V + 127) // 128, T, 2, dtype=torch.float32, device=DEV)
+    out = torch.empty(T, 2, dtype=torch.float32, device=DEV)
+    ops.lm_head_argmax(x, w, 0, tiles, out)
+    torch.cuda.synchronize()
+    idx = out[:, 1].contiguous().view(torch.int32).long()
+    picked = logits.gather(1, idx[:, None])[:, 0]
+    # the chosen entry is the max up to bf16 rounding of the accumulated logits
+    assert bool((picked >= logits.max(-1).values - 2e-2 * logits.abs().max()).all())
+
+
+@pytest.mark.parametrize("trans", [False, True])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_whole_tile_epilogue_strided_out(trans, epi):
+    """Whole-tile (data-parallel) epilogue into a column slice of a wider tensor: an output pitch
+    that is not a multiple of 16 bytes takes the scalar store path."""
+    T, N, K = 200, 512, 256
+    x = _rand(T, K, seed=25)
+    w = _rand(N, K, std=0.05, seed=26)
+    want = x.float() @ w.float().T
+    if epi == 2:
+        want = ref.silu_mul_interleaved(want)
+    n_out = want.shape[1]
+    dt = torch.float32 if epi == 1 else torch.bfloat16
+    big = torch.zeros(T, n_out + 3, dtype=dt, device=DEV)
+    out = big[:, 1:1 + n_out]
+    A, B = (w, x) if trans else (x, w)
+    ops.gemm(A, B, out, epi, trans=trans, mode=1)
+    torch.cuda.synchronize()
+    assert rel_err(out, want) < (2e-3 if epi == 1 else 1e-2)
+    assert float(big[:, 0].abs().max()) == 0.0 and float(big[:, -2:].abs().max()) == 0.0
+
+
 def test_linear_both_orientations_agree():
     x = _rand(100, 512, seed=7)
     w = _rand(640, 512, std=0.05, seed=8)

@@ -1,4 +1,5 @@
-"""Tensor-parallel paths on 2 GPUs, run as spawned child processes (NCCL for plumbing, NVLS off).
+"""Tensor-parallel paths on 2 GPUs, run as spawned child processes (NCCL for plumbing with its NVLS
+off; the fused kernels on plain peer loads, except the test that checks their NVLS multicast path).
 
 * the fused peer-memory all-reduce + residual + RMSNorm kernel (one-shot and two-shot) against an
   fp32 reference built from NCCL all-gathered partials;
@@ -32,12 +33,17 @@ def _run(fn, world, *args):
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
         mp.spawn(_entry, args=(world, port, fn, d, args), nprocs=world, join=True)
-        errs = []
+        errs, skips = [], []
         for r in range(world):
             f = os.path.join(d, f"err{r}")
             if os.path.exists(f):
                 errs.append(open(f).read())
+            f = os.path.join(d, f"skip{r}")
+            if os.path.exists(f):
+                skips.append(open(f).read())
         assert not errs, "\n".join(errs)
+        if skips:
+            pytest.skip(skips[0])
 
 
 def _entry(rank, world, port, fn, d, args):
@@ -46,10 +52,15 @@ def _entry(rank, world, port, fn, d, args):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+    # rendezvous through a file in the test's private directory: no TCP port to race for
+    dist.init_process_group("nccl", init_method=f"file://{os.path.join(d, 'pg_store')}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        fn(rank, world, *args)
+        reason = fn(rank, world, *args)
+        if isinstance(reason, str):
+            with open(os.path.join(d, f"skip{rank}"), "w") as f:
+                f.write(reason)
     except Exception:
         with open(os.path.join(d, f"err{rank}"), "w") as f:
             f.write(f"rank {rank}:\n" + traceback.format_exc())
@@ -62,14 +73,16 @@ def _entry(rank, world, port, fn, d, args):
         dist.destroy_process_group()
 
 
-def _ar_check(rank, world):
+def _ar_check(rank, world, multicast=False):
     import torch.distributed as dist
     from mesh_b200 import ops
     from mesh_b200.ops import reference as ref
     from mesh_b200.parallel.symm import SymmWorkspace
     dev = torch.device("cuda", rank)
     H = 4096
-    ws = SymmWorkspace(1024, H, dev)
+    ws = SymmWorkspace(1024, H, dev, multicast=multicast)
+    if multicast and not ws.mc_base:
+        return "symmetric memory has no NVLS multicast mapping on this node"
     gamma = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(1))).to(torch.bfloat16).to(dev)
     parity = 0
     for T in (1, 7, 64, 300, 1024):
@@ -78,7 +91,7 @@ def _ar_check(rank, world):
             part = torch.randn(T, H, generator=torch.Generator().manual_seed(100 * T + rank)).to(torch.bfloat16).to(dev)
             ws.resid(T).copy_(resid0)
             ws.partial(parity, T).copy_(part)
-            ws.fused_allreduce_norm(T, parity, gamma, 1e-5, two_shot=two_shot, timeout_s=5.0)
+            ws.fused_allreduce_norm(T, parity, gamma, 1e-5, two_shot=two_shot, timeout_s=5.0, multicast=multicast)
             torch.cuda.synchronize()
             ops.scratch(dev).check("ar")
             allp = torch.empty(world, T, H, dtype=torch.bfloat16, device=dev)
@@ -133,7 +146,7 @@ def _timeout_check(rank, world):
     from mesh_b200.parallel.symm import SymmWorkspace
     dev = torch.device("cuda", rank)
     H = 1024
-    ws = SymmWorkspace(64, H, dev)
+    ws = SymmWorkspace(64, H, dev, multicast=False)  # fault-path tests use plain peer loads only
     gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
     dist.barrier()
     if rank == 0:
@@ -204,6 +217,10 @@ def _need_gpus():
 
 def test_fused_allreduce_norm_2gpu():
     _run(_ar_check, 2)
+
+
+def test_fused_allreduce_norm_nvls_2gpu():
+    _run(_ar_check, 2, True)
 
 
 def test_fused_gemm_reduce_scatter_push_2gpu():
