@@ -59,6 +59,7 @@ struct GemmParams {
   int epi_bytes;      // shared memory of the epilogue region (staging, or split-K receive buffers)
   int vec_out;        // output rows start 16-byte aligned: whole-tile epilogue may store 16 bytes at once
   int direct_epi;     // whole tiles go TMEM -> registers -> global (else staged through shared memory)
+  int kbox;           // 64-wide k boxes per pipeline stage (1 or 2); a k-block is 64 * kbox wide
   void* out;
   long ldo;
   float* workspace;   // stream-K partial tiles: slot (sk_tile + cta) x [BM][bn] fp32
@@ -118,9 +119,9 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
   b = (b + 1023) & ~uintptr_t(1023);
   uint8_t* ptr = reinterpret_cast<uint8_t*>(b);
   s.a = ptr;
-  ptr += (size_t)p.stages * A_STAGE_BYTES;
+  ptr += (size_t)p.stages * A_STAGE_BYTES * p.kbox;
   s.b = ptr;
-  ptr += (size_t)p.stages * p.bn * BK * 2;
+  ptr += (size_t)p.stages * p.bn * BK * 2 * p.kbox;
   s.epi = reinterpret_cast<float*>(ptr);
   ptr += p.epi_bytes;
   ptr = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ptr) + 7) & ~uintptr_t(7));
@@ -138,8 +139,8 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const GemmParams& p) {
 constexpr int EPI_STAGING_BYTES = 2 * EPI_SLOT_FLOATS * (int)sizeof(float);
 constexpr size_t SMEM_BUDGET = 232448;
 
-__host__ __device__ inline size_t gemm_smem_bytes(int stages, int bn, int epi_bytes = EPI_STAGING_BYTES) {
-  return 1024 + (size_t)stages * (A_STAGE_BYTES + bn * BK * 2) + (size_t)epi_bytes + 8 +
+__host__ __device__ inline size_t gemm_smem_bytes(int stages, int bn, int epi_bytes = EPI_STAGING_BYTES, int kbox = 1) {
+  return 1024 + (size_t)stages * (A_STAGE_BYTES + bn * BK * 2) * kbox + (size_t)epi_bytes + 8 +
          (size_t)(2 * stages + 5) * 8 + 16;
 }
 
@@ -417,9 +418,12 @@ __device__ __forceinline__ void tmem_chunk_to_smem(uint32_t taddr_row, int col, 
 // warp: the up warps hand their chunk over in shared memory (double-buffered). The greedy-head
 // epilogue reduces (max, first index) per token over the 128 rows with warp shuffles and a
 // 4-entry cross-warp step. The TMEM buffer is released right after its last column is read.
+// `fetch(col, r)` produces the 16 fp32 accumulator values of this thread's row at columns
+// [col, col + 16): straight from TMEM for whole tiles, or TMEM plus the other contributors'
+// partials (added in fixed order) for a stream-K tile's owner.
 // ----------------------------------------------------------------------------------------------
-template <int EPI, bool TRANS>
-__device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem& s, uint32_t taddr_row, int row,
+template <int EPI, bool TRANS, typename Fetch>
+__device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem& s, Fetch&& fetch, int row,
                                                 int lane, int quarter, int tm, int tn, uint64_t* tempty) {
   const int m_base = tm * BM;
   const int nchunks = (p.bn + 15) / 16;
@@ -438,9 +442,8 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     for (int c = 0; c < p.bn / 2; c += 16) {
       const int g = c / 64, j0 = c % 64;
       uint32_t rg[16], ru[16];
-      tmem_ld16(taddr_row + g * 128 + j0, rg);
-      tmem_ld16(taddr_row + g * 128 + 64 + j0, ru);
-      tmem_ld_wait();
+      fetch(g * 128 + j0, rg);
+      fetch(g * 128 + 64 + j0, ru);
       if (c + 16 >= p.bn / 2) {
         tc_fence_before();
         mbar_arrive(tempty);
@@ -468,8 +471,7 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     const int m_out = tm * (BM / 2) + q;
     for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
       uint32_t r[16];
-      tmem_ld16(taddr_row + c, r);
-      tmem_ld_wait();
+      fetch(c, r);
       release_if_last(c);
       float* xb = xbuf + (chunk_i & 1) * (64 * 17) + q * 17;
       if (up) {
@@ -490,8 +492,7 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     const int m = m_base + row;
     for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
       uint32_t r[16];
-      tmem_ld16(taddr_row + c, r);
-      tmem_ld_wait();
+      fetch(c, r);
       release_if_last(c);
       float* rv = xbuf + (chunk_i & 1) * 128;  // [4 quarters][16 tokens] values, then indices
       int* ri = reinterpret_cast<int*>(rv + 64);
@@ -534,8 +535,7 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     const int m = m_base + row;
     for (int c = 0; c < p.bn; c += 16) {
       uint32_t r[16];
-      tmem_ld16(taddr_row + c, r);
-      tmem_ld_wait();
+      fetch(c, r);
       release_if_last(c);
       if (m >= p.M) continue;
 #pragma unroll
@@ -552,8 +552,7 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     const int m = m_base + row;
     for (int c = 0; c < p.bn; c += 16) {
       uint32_t r[16];
-      tmem_ld16(taddr_row + c, r);
-      tmem_ld_wait();
+      fetch(c, r);
       release_if_last(c);
       const int n0 = tn * p.bn + c;
       if (m >= p.M) continue;
@@ -747,7 +746,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   Smem s = carve(smem_raw, p);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t b_stage_bytes = (uint32_t)p.bn * BK * 2;
+  const int kbox = p.kbox;
+  const uint32_t a_box_bytes = A_STAGE_BYTES, b_box_bytes = (uint32_t)p.bn * BK * 2;
+  const uint32_t a_stage_bytes = a_box_bytes * kbox, b_stage_bytes = b_box_bytes * kbox;
+  const int bk_eff = BK * kbox;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
@@ -802,13 +804,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           first_seg = false;
           const int npre = min(p.stages, sg.kb1 - sg.kb0);
           for (int i = 0; i < npre; ++i) {
-            mbar_arrive_expect_tx(&s.full[i], A_STAGE_BYTES + b_stage_bytes);
-            tma_load_2d(s.a + (size_t)i * A_STAGE_BYTES, &tmA, &s.full[i], (sg.kb0 + i) * BK, sg.tm * BM, pol_a);
+            mbar_arrive_expect_tx(&s.full[i], a_stage_bytes + b_stage_bytes);
+            for (int j = 0; j < kbox; ++j)
+              tma_load_2d(s.a + (size_t)i * a_stage_bytes + j * a_box_bytes, &tmA, &s.full[i],
+                          (sg.kb0 + i) * bk_eff + j * BK, sg.tm * BM, pol_a);
           }
           griddep_wait();
           if (trace) trace[1] = globaltimer_ns();
           for (int i = 0; i < npre; ++i)
-            tma_load_2d(s.b + (size_t)i * b_stage_bytes, &tmB, &s.full[i], (sg.kb0 + i) * BK, sg.tn * p.bn, pol_b);
+            for (int j = 0; j < kbox; ++j)
+              tma_load_2d(s.b + (size_t)i * b_stage_bytes + j * b_box_bytes, &tmB, &s.full[i],
+                          (sg.kb0 + i) * bk_eff + j * BK, sg.tn * p.bn, pol_b);
           kb_start = sg.kb0 + npre;
           stage = npre % p.stages;
           phase = (npre == p.stages) ? 1u : 0u;
@@ -819,9 +825,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&s.full[stage], A_STAGE_BYTES + b_stage_bytes);
-          tma_load_2d(s.a + (size_t)stage * A_STAGE_BYTES, &tmA, &s.full[stage], kb * BK, sg.tm * BM, pol_a);
-          tma_load_2d(s.b + (size_t)stage * b_stage_bytes, &tmB, &s.full[stage], kb * BK, sg.tn * p.bn, pol_b);
+          mbar_arrive_expect_tx(&s.full[stage], a_stage_bytes + b_stage_bytes);
+          for (int j = 0; j < kbox; ++j) {
+            tma_load_2d(s.a + (size_t)stage * a_stage_bytes + j * a_box_bytes, &tmA, &s.full[stage],
+                        kb * bk_eff + j * BK, sg.tm * BM, pol_a);
+            tma_load_2d(s.b + (size_t)stage * b_stage_bytes + j * b_box_bytes, &tmB, &s.full[stage],
+                        kb * bk_eff + j * BK, sg.tn * p.bn, pol_b);
+          }
           if (++stage == p.stages) {
             stage = 0;
             phase ^= 1;
@@ -878,14 +888,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         if (trace && lane == 0 && it == 0 && kb == sg.kb0) trace[3] = globaltimer_ns();
         if (lane == 0) {
-          const uint32_t a_addr = smem_u32(s.a + (size_t)stage * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(s.b + (size_t)stage * b_stage_bytes);
-          const uint64_t a_desc = make_sdesc_sw128(a_addr);
-          const uint64_t b_desc = make_sdesc_sw128(b_addr);
+          for (int j = 0; j < kbox; ++j) {
+            const uint32_t a_addr = smem_u32(s.a + (size_t)stage * a_stage_bytes + j * a_box_bytes);
+            const uint32_t b_addr = smem_u32(s.b + (size_t)stage * b_stage_bytes + j * b_box_bytes);
+            const uint64_t a_desc = make_sdesc_sw128(a_addr);
+            const uint64_t b_desc = make_sdesc_sw128(b_addr);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // advance 16 bf16 = 32 bytes inside the swizzled 128-byte row: +2 in 16-byte units
-            umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, p.idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k) {
+              // advance 16 bf16 = 32 bytes inside the swizzled 128-byte row: +2 in 16-byte units
+              umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, p.idesc,
+                        (kb > sg.kb0 || j > 0 || k > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&s.empty[stage]);
         }
@@ -939,8 +952,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t taddr_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
 
+      auto fetch_tmem = [&](int col, uint32_t (&r)[16]) {
+        tmem_ld16(taddr_row + col, r);
+        tmem_ld_wait();
+      };
       if (sg.ncontrib == 1 && p.push_mode == 0 && p.direct_epi) {
-        direct_epilogue<EPI, TRANS>(p, s, taddr_row, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
+        direct_epilogue<EPI, TRANS>(p, s, fetch_tmem, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
+      } else if (sg.ncontrib > 1 && sg.contrib == 0 && p.push_mode == 0 && p.direct_epi) {
+        // stream-K owner: wait (bounded) for the other contributors' partials, then run the
+        // whole-tile epilogue on own accumulator + partials, read per row straight from the
+        // workspace in contributor order (deterministic)
+        const bool okw = wait_counter_eq(&p.counters[sg.sk_tile], sg.ncontrib - 1, WAIT_LIMIT_NS, p.err,
+                                         ERR_MBAR_TIMEOUT_EPILOGUE);
+        (void)okw;
+        named_bar_sync(1, 128);
+        if (et == 0) p.counters[sg.sk_tile] = 0;
+        if (trace && et == 0) trace[10] = globaltimer_ns();
+        const float* part_row = p.workspace + (size_t)(sg.sk_tile + sg.first_cta + 1) * tile_floats +
+                                (size_t)row * p.bn;
+        const int nparts = sg.ncontrib - 1;
+        auto fetch_sum = [&](int col, uint32_t (&r)[16]) {
+          tmem_ld16(taddr_row + col, r);
+          float4 y[4];
+          float a[16];
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) a[i] = __uint_as_float(r[i]);
+          for (int k = 0; k < nparts; ++k) {
+            const float4* src = reinterpret_cast<const float4*>(part_row + (size_t)k * tile_floats + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) y[i] = __ldcg(src + i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              a[4 * i] += y[i].x; a[4 * i + 1] += y[i].y; a[4 * i + 2] += y[i].z; a[4 * i + 3] += y[i].w;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(a[i]);
+        };
+        direct_epilogue<EPI, TRANS>(p, s, fetch_sum, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
+        if (trace && et == 0) trace[11] = globaltimer_ns();
       } else if (sg.ncontrib == 1) {
         const int nsteps = ChunkPlan<EPI, TRANS>::steps(p.bn);
         for (int st = 0; st < nsteps; ++st) {
@@ -992,7 +1043,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (et == 0) p.counters[sg.sk_tile] = 0;
           if (trace && et == 0) trace[10] = globaltimer_ns();
           const uint32_t tile_bytes = (uint32_t)(tile_floats * 4);
-          const size_t ring_bytes = (size_t)p.stages * (A_STAGE_BYTES + b_stage_bytes);
+          const size_t ring_bytes = (size_t)p.stages * (a_stage_bytes + b_stage_bytes);
           const int per_batch = (int)(ring_bytes / tile_bytes) < 1 ? 1 : (int)(ring_bytes / tile_bytes);
           const float* part0 = p.workspace + (size_t)(sg.sk_tile + sg.first_cta) * tile_floats;
           const int nsteps = ChunkPlan<EPI, TRANS>::steps(p.bn);
@@ -1204,19 +1255,31 @@ static int max_stages() {
   return v;
 }
 
-static SmemPlan smem_plan(int bn, int C) {
+// 64-wide k boxes per pipeline stage: decode (swap-AB, weight streaming) moves 32 KB of weights
+// per stage, which sustains a higher per-SM rate than 16 KB stages (fewer barrier round trips per
+// byte); prefill keeps 64-wide stages so that more of them fit next to the 256-wide B tiles.
+static int kbox_for(bool trans) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESH_GEMM_KBOX");
+    v = e ? std::max(1, std::min(2, std::atoi(e))) : 0;
+  }
+  return v > 0 ? v : (trans ? 2 : 1);
+}
+
+static SmemPlan smem_plan(int bn, int C, int kbox) {
   SmemPlan sp;
   sp.epi_bytes = C > 1 ? std::max(EPI_STAGING_BYTES, ck_recv_bytes(bn, C)) : EPI_STAGING_BYTES;
   sp.stages = max_stages();
-  while (sp.stages > 2 && gemm_smem_bytes(sp.stages, bn, sp.epi_bytes) > SMEM_BUDGET) --sp.stages;
-  sp.bytes = gemm_smem_bytes(sp.stages, bn, sp.epi_bytes);
+  while (sp.stages > 2 && gemm_smem_bytes(sp.stages, bn, sp.epi_bytes, kbox) > SMEM_BUDGET) --sp.stages;
+  sp.bytes = gemm_smem_bytes(sp.stages, bn, sp.epi_bytes, kbox);
   return sp;
 }
 
-static int pick_ck(int tiles, int kb, int num_sms, int epi, int bn) {
+static int pick_ck(int tiles, int kb, int num_sms, int epi, int bn, int kbox) {
   int C = std::min(16, std::min(kb, num_sms / std::max(tiles, 1)));
   for (; C >= 2; --C) {
-    const SmemPlan sp = smem_plan(bn, C);
+    const SmemPlan sp = smem_plan(bn, C, kbox);
     if (sp.bytes <= SMEM_BUDGET && max_active_clusters_for(epi, true, C, sp.bytes) >= tiles) return C;
   }
   return 0;
@@ -1243,16 +1306,24 @@ struct Plan {
 };
 
 // force_mode: 0 auto, 1 data-parallel, 2 stream-K, 3 cluster split-K (swap-AB only).
-static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode, int epi = 0, bool trans = false,
-                      bool push = false) {
+static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode, int epi, bool trans, bool push,
+                      int kbox) {
   Plan pl{};
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + bn - 1) / bn;
-  const int kb = (K + BK - 1) / BK;
+  const int kb = (K + BK * kbox - 1) / (BK * kbox);
   pl.tiles = m_tiles * n_tiles;
   const long total_iters = (long)pl.tiles * kb;
   int grid = num_sms;
+  // Automatic choice for swap-AB (decode) shapes, from measured decode sweeps: one wave of whole
+  // tiles when they fill most SMs or each tile is short (<= 8 k-blocks, where a split's fixed
+  // cost outweighs its parallelism); cluster split-K when the tiles leave SMs idle.
+  if (trans && force_mode == 0 && pl.tiles <= num_sms && (4 * pl.tiles >= 3 * num_sms || kb <= 8)) {
+    pl.grid = pl.tiles;
+    pl.dp_tiles = pl.tiles;
+    return pl;
+  }
   if (trans && !push && (force_mode == 3 || (force_mode == 0 && ck_enabled() && pl.tiles < num_sms))) {
-    const int C = pick_ck(pl.tiles, kb, num_sms, epi, bn);
+    const int C = pick_ck(pl.tiles, kb, num_sms, epi, bn, kbox);
     if (C >= 2) {
       pl.ck = C;
       pl.grid = pl.tiles * C;
@@ -1319,13 +1390,15 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   p.bn = bn;
   p.m_tiles = (M + BM - 1) / BM;
   p.n_tiles = (N + bn - 1) / bn;
-  p.k_blocks = (K + BK - 1) / BK;
+  const int kbox = kbox_for(trans);
+  p.kbox = kbox;
+  p.k_blocks = (K + BK * kbox - 1) / (BK * kbox);
   const int sms = num_sms_cached(dev);
-  Plan pl = make_plan(M, N, K, bn, sms, (int)mode, (int)epi, trans, !push.empty());
+  Plan pl = make_plan(M, N, K, bn, sms, (int)mode, (int)epi, trans, !push.empty(), kbox);
   p.ck = pl.ck;
   TORCH_CHECK(mode != 3 || pl.ck >= 2, "gemm_tcgen05: cluster split-K requested but not possible for this shape");
   TORCH_CHECK(p.ck <= 1 || (trans && push.empty()), "gemm_tcgen05: cluster split-K needs swap-AB and no push");
-  const SmemPlan sp = smem_plan(bn, p.ck);
+  const SmemPlan sp = smem_plan(bn, p.ck, kbox);
   TORCH_CHECK(sp.bytes <= SMEM_BUDGET, "gemm_tcgen05: shared memory plan exceeds the budget");
   const int stages = sp.stages;
   p.epi_bytes = sp.epi_bytes;
@@ -1390,8 +1463,9 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device) {
   const c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
   int bn = gemm_pick_bn((int)N, (int)epi, trans);
-  Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0, (int)epi, trans, false);
-  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, smem_plan(bn, pl.ck).stages, pl.grid, pl.dp_tiles, pl.sk_iters,
+  const int kbox = kbox_for(trans);
+  Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0, (int)epi, trans, false, kbox);
+  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, smem_plan(bn, pl.ck, kbox).stages, pl.grid, pl.dp_tiles, pl.sk_iters,
           pl.ck};
 }
 
