@@ -145,7 +145,9 @@ class EngineConfig:
     prefill_chunk_tokens: int = 16384
     use_fused_allreduce: bool = True
     allreduce_impl: str = "auto"  # auto | oneshot | twoshot | push | push_oneshot | nccl
-    nvls: bool = True  # fused all-reduce through NVSwitch multicast (multimem) when the node has it
+    # fused all-reduce through NVSwitch multicast (multimem loads/stores) when the node has it; off by
+    # default: on 2 and 8 B200s the plain peer-load kernel measured faster at every size
+    nvls: bool = False
     extra: dict = field(default_factory=dict)
 
     def bucket_for(self, batch: int) -> int:

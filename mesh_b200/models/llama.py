@@ -107,7 +107,12 @@ class LlamaRunner:
             return True
         if self.push_rs:
             return T >= self.world  # pushing to the owner moves each row once; all-gather follows
-        return T * self.H * 2 * (self.world - 1) > (1 << 20)  # > ~1 MiB read per rank: two-shot
+        # one-shot reads every peer's full partial (T*H*2*(world-1) bytes per rank) behind one barrier;
+        # two-shot moves 1/world of that each way behind two. Measured crossover on B200: two ranks
+        # never (one-shot won up to T=4096 at H=4096), eight ranks between T=64 and T=512 at H=4096.
+        if self.world <= 2:
+            return False
+        return T * self.H * 2 * (self.world - 1) > (8 << 20)
 
     def _reduce(self, part: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor, gamma: torch.Tensor,
                 parity: int):
