@@ -409,28 +409,63 @@ __device__ __forceinline__ void tmem_chunk_to_smem(uint32_t taddr_row, int col, 
 // columns over the C sources in source order (deterministic) from local shared memory and runs
 // the epilogue. Both barriers are reached on every path, errors included.
 // ----------------------------------------------------------------------------------------------
+// Swap-AB bf16 output through shared memory: the tile's rows are output features and its columns
+// tokens, so a thread holds one feature of many tokens; written straight to global memory that is
+// one 2-byte store per token per thread, which measured ~25 ns each (1.6 us for a 64-token tile).
+// Instead each thread puts its values into a [ncols tokens][fw features] bf16 staging tile
+// (conflict-free: a warp writes 64 contiguous bytes), and after a named barrier the 128 epilogue
+// threads write whole 16-byte chunks of token rows (a warp covers 2-4 rows of 128-256 contiguous
+// bytes). `f0` is the first output feature of the tile, `n0` its first token.
+__device__ __forceinline__ void stage_put_bf16(uint32_t stage, int fw, int j, int f, float v) {
+  __nv_bfloat16 b = f2bf(v);
+  sts_u16(stage + (uint32_t)(j * fw + f) * 2, *reinterpret_cast<uint16_t*>(&b));
+}
+__device__ __forceinline__ void stage_flush_bf16(const GemmParams& p, uint32_t stage, int fw, int ncols, int n0,
+                                                 int f0, int f_lim, int et) {
+  named_bar_sync(1, 128);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+  const int cpr = fw / 8;  // 16-byte chunks per token row
+  for (int k = et; k < ncols * cpr; k += 128) {
+    const int j = k / cpr, c8 = (k - j * cpr) * 8;
+    const int n = n0 + j, f = f0 + c8;
+    if (n >= p.N || f >= f_lim) continue;
+    const uint4 v = lds_u4(stage + (uint32_t)(j * fw + c8) * 2);
+    __nv_bfloat16* dst = out + (long)n * p.ldo + f;
+    if (p.vec_out && f + 8 <= f_lim) {
+      *reinterpret_cast<uint4*>(dst) = v;
+    } else {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+      for (int i = 0; i < 8 && f + i < f_lim; ++i) dst[i] = e[i];
+    }
+  }
+  named_bar_sync(1, 128);  // staging tile free for the next block
+}
+
 // ----------------------------------------------------------------------------------------------
 // Whole-tile epilogue straight from TMEM to global memory (no shared-memory staging): each thread
 // owns one accumulator row (TMEM lane). Swap-AB: the row is an output feature and its columns are
 // tokens, so for every token the 32 lanes of a warp write 32 consecutive features (64 B bf16).
-// Normal orientation: the row is a token and its 16-column chunks are 32 contiguous bytes, written
+// Normal orientation: the row is a token and its 16-column groups are 32 contiguous bytes, written
 // as 16-byte vectors. SiLU in swap-AB pairs gate row r with up row r + 64, which lives in another
-// warp: the up warps hand their chunk over in shared memory (double-buffered). The greedy-head
+// warp: the up warps hand their columns over in shared memory (double-buffered). The greedy-head
 // epilogue reduces (max, first index) per token over the 128 rows with warp shuffles and a
-// 4-entry cross-warp step. The TMEM buffer is released right after its last column is read.
-// `fetch(col, r)` produces the 16 fp32 accumulator values of this thread's row at columns
-// [col, col + 16): straight from TMEM for whole tiles, or TMEM plus the other contributors'
-// partials (added in fixed order) for a stream-K tile's owner.
+// 4-entry cross-warp step. Columns are read from TMEM up to 64 at a time behind a single
+// tcgen05.wait (a wait per 16 columns cost ~2 us per tile); the buffer is released right after
+// its last column is read.
+// `fetch(col, r, n16)` fills r[0 .. 16*n16) with this thread's row at columns [col, col + 16*n16):
+// straight from TMEM for whole tiles, or TMEM plus the other contributors' partials (added in a
+// fixed order) for a stream-K tile's owner.
 // ----------------------------------------------------------------------------------------------
 template <int EPI, bool TRANS, typename Fetch>
 __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem& s, Fetch&& fetch, int row,
                                                 int lane, int quarter, int tm, int tn, uint64_t* tempty) {
   const int m_base = tm * BM;
-  const int nchunks = (p.bn + 15) / 16;
-  float* xbuf = s.epi;  // SiLU hand-over [2][64][17] / argmax partials [2][4][16] x (value, index)
-  int chunk_i = 0;
-  auto release_if_last = [&](int c) {
-    if (c + 16 >= p.bn) {
+  // SiLU hand-over [2][2][64][17] words + output staging [64][64] bf16 / argmax partials [2][4][64] x
+  // (value, index) / swap-AB bf16 output staging [64][128]
+  float* xbuf = s.epi;
+  int blk = 0;
+  auto release_if_last = [&](int c_end) {
+    if (c_end >= p.bn) {
       tc_fence_before();
       mbar_arrive(tempty);
     }
@@ -439,65 +474,96 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     // gate columns g*128 + [0, 64), up columns g*128 + 64 + [0, 64); output column tn*bn/2 + g*64 + j
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
     const int m = m_base + row;
-    for (int c = 0; c < p.bn / 2; c += 16) {
+    for (int c = 0; c < p.bn / 2; c += 32) {
       const int g = c / 64, j0 = c % 64;
-      uint32_t rg[16], ru[16];
-      fetch(g * 128 + j0, rg);
-      fetch(g * 128 + 64 + j0, ru);
-      if (c + 16 >= p.bn / 2) {
+      uint32_t rg[32], ru[32];
+      fetch(g * 128 + j0, rg, 2);
+      fetch(g * 128 + 64 + j0, ru, 2);
+      if (c + 32 >= p.bn / 2) {
         tc_fence_before();
         mbar_arrive(tempty);
       }
-      const int n0 = tn * (p.bn / 2) + c;
       if (m >= p.M) continue;
-      uint32_t pk[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        pk[i] = pack_bf16x2(silu_f(__uint_as_float(rg[2 * i])) * __uint_as_float(ru[2 * i]),
-                            silu_f(__uint_as_float(rg[2 * i + 1])) * __uint_as_float(ru[2 * i + 1]));
-      __nv_bfloat16* dst = out + (long)m * p.ldo + n0;
-      if (p.vec_out && n0 + 16 <= p.N / 2) {
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      } else {
-        for (int i = 0; i < 16 && n0 + i < p.N / 2; ++i)
-          dst[i] = f2bf(silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]));
+      for (int h = 0; h < 2; ++h) {
+        const int n0 = tn * (p.bn / 2) + c + 16 * h;
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pk[i] = pack_bf16x2(silu_f(__uint_as_float(rg[16 * h + 2 * i])) * __uint_as_float(ru[16 * h + 2 * i]),
+                              silu_f(__uint_as_float(rg[16 * h + 2 * i + 1])) * __uint_as_float(ru[16 * h + 2 * i + 1]));
+        __nv_bfloat16* dst = out + (long)m * p.ldo + n0;
+        if (p.vec_out && n0 + 16 <= p.N / 2) {
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+          for (int i = 0; i < 16 && n0 + i < p.N / 2; ++i)
+            dst[i] = f2bf(silu_f(__uint_as_float(rg[16 * h + i])) * __uint_as_float(ru[16 * h + i]));
+        }
       }
     }
   } else if constexpr (EPI == EPI_SILU_BF16 && TRANS) {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
     const bool up = row >= 64;
     const int q = row & 63;
-    const int m_out = tm * (BM / 2) + q;
-    for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
-      uint32_t r[16];
-      fetch(c, r);
-      release_if_last(c);
-      float* xb = xbuf + (chunk_i & 1) * (64 * 17) + q * 17;
+    for (int c = 0; c < p.bn; c += 64, ++blk) {
+      const int n16 = min(4, (p.bn - c + 15) / 16);
+      uint32_t r[64];
+      fetch(c, r, n16);
+      release_if_last(c + 64);
+      // Balanced exchange: gate thread q keeps columns [0, 32) of the block and receives the matching
+      // "up" values; up thread q keeps columns [32, 64) and receives the matching gate values. Values
+      // cross as bf16 pairs ([2 dirs][64 features][17 words]); the product is rounded to bf16 anyway.
+      uint32_t* xg = reinterpret_cast<uint32_t*>(xbuf) + (blk & 1) * (2 * 64 * 17);  // gate -> up warps
+      uint32_t* xu = xg + 64 * 17;                                                 // up -> gate warps
+      // (register indices stay compile-time constants in both branches: no local-memory arrays)
+      const uint32_t stg = smem_u32(reinterpret_cast<uint32_t*>(xbuf) + 4 * 64 * 17);  // [64 tokens][64] bf16
       if (up) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) xb[j] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; j += 2)
+          xu[q * 17 + j / 2] = pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          xg[q * 17 + j / 2] = pack_bf16x2(__uint_as_float(r[32 + j]), __uint_as_float(r[32 + j + 1]));
       }
       named_bar_sync(1, 128);
-      if (!up && m_out < p.M / 2) {
+      if (up) {  // columns [32, 64): own up values, gate values received
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = tn * p.bn + c + j;
-          if (n < p.N) out[(long)n * p.ldo + m_out] = f2bf(silu_f(__uint_as_float(r[j])) * xb[j]);
+        for (int j = 0; j < 32; j += 2) {
+          if (32 + j < 16 * n16) {
+            float g0, g1;
+            unpack_bf16x2(xg[q * 17 + j / 2], g0, g1);
+            stage_put_bf16(stg, 64, 32 + j, q, silu_f(g0) * __uint_as_float(r[32 + j]));
+            stage_put_bf16(stg, 64, 32 + j + 1, q, silu_f(g1) * __uint_as_float(r[32 + j + 1]));
+          }
+        }
+      } else {   // columns [0, 32): own gate values, up values received
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          if (j < 16 * n16) {
+            float u0, u1;
+            unpack_bf16x2(xu[q * 17 + j / 2], u0, u1);
+            stage_put_bf16(stg, 64, j, q, silu_f(__uint_as_float(r[j])) * u0);
+            stage_put_bf16(stg, 64, j + 1, q, silu_f(__uint_as_float(r[j + 1])) * u1);
+          }
         }
       }
+      stage_flush_bf16(p, stg, 64, 16 * n16, tn * p.bn + c, tm * (BM / 2), p.M / 2, threadIdx.x - 64);
     }
   } else if constexpr (EPI == EPI_ARGMAX) {
     static_assert(TRANS, "argmax epilogue runs in swap-AB orientation");
     const int m = m_base + row;
-    for (int c = 0; c < p.bn; c += 16, ++chunk_i) {
-      uint32_t r[16];
-      fetch(c, r);
-      release_if_last(c);
-      float* rv = xbuf + (chunk_i & 1) * 128;  // [4 quarters][16 tokens] values, then indices
-      int* ri = reinterpret_cast<int*>(rv + 64);
+    const int et = (threadIdx.x - 64);
+    for (int c = 0; c < p.bn; c += 64, ++blk) {
+      const int n16 = min(4, (p.bn - c + 15) / 16);
+      uint32_t r[64];
+      fetch(c, r, n16);
+      release_if_last(c + 64);
+      float* rv = xbuf + (blk & 1) * 512;  // [4 quarters][64 tokens] values, then indices
+      int* ri = reinterpret_cast<int*>(rv + 256);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 64; ++j) {
+        if (j >= 16 * n16) break;
         float best = (m < p.M) ? __uint_as_float(r[j]) : -INFINITY;
         int bi = (m < p.M) ? m : 0x7fffffff;
 #pragma unroll
@@ -510,18 +576,17 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
           }
         }
         if (lane == 0) {
-          rv[quarter * 16 + j] = best;
-          ri[quarter * 16 + j] = bi;
+          rv[quarter * 64 + j] = best;
+          ri[quarter * 64 + j] = bi;
         }
       }
       named_bar_sync(1, 128);
-      const int et = (threadIdx.x - 64);
-      if (et < 16) {
+      if (et < 16 * n16) {
         float best = rv[et];
         int bi = ri[et];
         for (int w = 1; w < 4; ++w) {
-          const float ov = rv[w * 16 + et];
-          const int oi = ri[w * 16 + et];
+          const float ov = rv[w * 64 + et];
+          const int oi = ri[w * 64 + et];
           if (ov > best || (ov == best && oi < bi)) {
             best = ov;
             bi = oi;
@@ -531,17 +596,30 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
         if (n < p.N) reinterpret_cast<float2*>(p.out)[(long)tm * p.ldo + n] = make_float2(best, __int_as_float(bi));
       }
     }
+  } else if constexpr (TRANS && EPI == EPI_STORE_BF16) {
+    const uint32_t stg = smem_u32(xbuf);  // [64 tokens][128 features] bf16
+    for (int c = 0; c < p.bn; c += 64) {
+      const int n16 = min(4, (p.bn - c + 15) / 16);
+      uint32_t r[64];
+      fetch(c, r, n16);
+      release_if_last(c + 64);
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (j < 16 * n16) stage_put_bf16(stg, BM, j, row, __uint_as_float(r[j]));
+      stage_flush_bf16(p, stg, BM, 16 * n16, tn * p.bn + c, m_base, p.M, threadIdx.x - 64);
+    }
   } else if constexpr (TRANS) {
     const int m = m_base + row;
-    for (int c = 0; c < p.bn; c += 16) {
-      uint32_t r[16];
-      fetch(c, r);
-      release_if_last(c);
+    for (int c = 0; c < p.bn; c += 64) {
+      const int n16 = min(4, (p.bn - c + 15) / 16);
+      uint32_t r[64];
+      fetch(c, r, n16);
+      release_if_last(c + 64);
       if (m >= p.M) continue;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 64; ++j) {
         const int n = tn * p.bn + c + j;
-        if (n >= p.N) break;
+        if (j >= 16 * n16 || n >= p.N) break;
         if constexpr (EPI == EPI_STORE_F32)
           reinterpret_cast<float*>(p.out)[(long)n * p.ldo + m] = __uint_as_float(r[j]);
         else
@@ -550,31 +628,38 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
     }
   } else {
     const int m = m_base + row;
-    for (int c = 0; c < p.bn; c += 16) {
-      uint32_t r[16];
-      fetch(c, r);
-      release_if_last(c);
-      const int n0 = tn * p.bn + c;
+    for (int c = 0; c < p.bn; c += 32) {
+      const int n16 = min(2, (p.bn - c + 15) / 16);
+      uint32_t r[32];
+      fetch(c, r, n16);
+      release_if_last(c + 32);
       if (m >= p.M) continue;
-      if constexpr (EPI == EPI_STORE_F32) {
-        float* dst = reinterpret_cast<float*>(p.out) + (long)m * p.ldo + n0;
-        if (p.vec_out && n0 + 16 <= p.N) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4*>(dst)[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-        } else {
-          for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = __uint_as_float(r[i]);
-        }
-      } else {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (long)m * p.ldo + n0;
-        if (p.vec_out && n0 + 16 <= p.N) {
-          uint32_t pk[8];
+      for (int h = 0; h < 2; ++h) {
+        if (h >= n16) break;
+        const int n0 = tn * p.bn + c + 16 * h;
+        if constexpr (EPI == EPI_STORE_F32) {
+          float* dst = reinterpret_cast<float*>(p.out) + (long)m * p.ldo + n0;
+          if (p.vec_out && n0 + 16 <= p.N) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<uint4*>(dst)[i] =
+                  make_uint4(r[16 * h + 4 * i], r[16 * h + 4 * i + 1], r[16 * h + 4 * i + 2], r[16 * h + 4 * i + 3]);
+          } else {
+            for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = __uint_as_float(r[16 * h + i]);
+          }
         } else {
-          for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = f2bf(__uint_as_float(r[i]));
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (long)m * p.ldo + n0;
+          if (p.vec_out && n0 + 16 <= p.N) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              pk[i] = pack_bf16x2(__uint_as_float(r[16 * h + 2 * i]), __uint_as_float(r[16 * h + 2 * i + 1]));
+            reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else {
+            for (int i = 0; i < 16 && n0 + i < p.N; ++i) dst[i] = f2bf(__uint_as_float(r[16 * h + i]));
+          }
         }
       }
     }
@@ -608,17 +693,21 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
   // this CTA's slot in any owner's buffer, at this thread's row
   const uint32_t my_slot_row = recv + rank * slot_bytes + (uint32_t)(row * ldr) * 4;
   cluster_wait_acquire();  // pairs with the arrive at kernel start: every peer CTA is running
-  for (int c = 0; c < p.bn; c += 16) {
-    uint32_t r[16];
+  for (int c = 0; c < p.bn; c += 64) {
+    const int n16 = min(4, (p.bn - c + 15) / 16);
+    uint32_t r[64];
     if (ok) {
-      tmem_ld16(taddr_row + c, r);
-      tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (k < n16) tmem_ld16(taddr_row + c + 16 * k, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * k]));
+      tmem_ld_wait_tied(r);
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) r[i] = 0u;
+      for (int i = 0; i < 64; ++i) r[i] = 0u;
     }
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
+    for (int i = 0; i < 64; i += 4) {
+      if (i >= 16 * n16) break;
       const int col = c + i;
       const int owner = col / cpc;
       const uint32_t local = my_slot_row + (uint32_t)(col - owner * cpc) * 4;
@@ -649,9 +738,9 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
   const int m_base = tm * BM;
   if constexpr (EPI == EPI_SILU_BF16) {
     // rows 0..63 gate, 64..127 up; the two thread halves take alternate 16-column groups
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    // staged [cpc tokens][64 features] bf16 in the idle operand ring, written as 16-byte chunks
+    const uint32_t stg = smem_u32(s.a);
     const int q = et & 63, half = et >> 6;
-    const int m_out = tm * (BM / 2) + q;
     for (int c = c_lo + 16 * half; c < c_hi; c += 32) {
       const int nv = min(4, (c_hi - c) >> 2);
       float4 g[8], u[8];
@@ -662,12 +751,10 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
         if (j >= nv) break;
         const float gv[4] = {g[j].x, g[j].y, g[j].z, g[j].w}, uv[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = tn * p.bn + c + 4 * j + e;
-          if (n < p.N && m_out < p.M / 2) out[(long)n * p.ldo + m_out] = f2bf(silu_f(gv[e]) * uv[e]);
-        }
+        for (int e = 0; e < 4; ++e) stage_put_bf16(stg, 64, c - c_lo + 4 * j + e, q, silu_f(gv[e]) * uv[e]);
       }
     }
+    if (c_hi > c_lo) stage_flush_bf16(p, stg, 64, c_hi - c_lo, tn * p.bn + c_lo, tm * (BM / 2), p.M / 2, et);
   } else if constexpr (EPI == EPI_ARGMAX) {
     // per token column: max over the tile's 128 rows (first index on ties) -> float2 [m_tiles][ldo]
     float* red_v = reinterpret_cast<float*>(s.a);  // operand ring: idle once this CTA's MMAs completed
@@ -712,13 +799,29 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
       }
       named_bar_sync(1, 128);
     }
+  } else if constexpr (EPI == EPI_STORE_BF16) {
+    // staged [cpc tokens][128 features] bf16 in the idle operand ring, written as 16-byte chunks
+    const uint32_t stg = smem_u32(s.a);
+    for (int c = c_lo; c < c_hi; c += 32) {
+      const int nv = min(8, (c_hi - c) >> 2);
+      float4 v[8];
+      sum_row(et, c, nv, v);
+      if (trace && et == 0 && c == c_lo) trace[11] = globaltimer_after(v[0].x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= nv) break;
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) stage_put_bf16(stg, BM, c - c_lo + 4 * j + e, et, vv[e]);
+      }
+    }
+    if (c_hi > c_lo) stage_flush_bf16(p, stg, BM, c_hi - c_lo, tn * p.bn + c_lo, m_base, p.M, et);
   } else {
     const int m = m_base + et;
     for (int c = c_lo; c < c_hi; c += 32) {
       const int nv = min(8, (c_hi - c) >> 2);
       float4 v[8];
       sum_row(et, c, nv, v);
-      if (trace && et == 0 && c == c_lo) trace[11] = globaltimer_after(v[0].x);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (j >= nv) break;
@@ -952,9 +1055,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t taddr_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
 
-      auto fetch_tmem = [&](int col, uint32_t (&r)[16]) {
-        tmem_ld16(taddr_row + col, r);
-        tmem_ld_wait();
+      // up to n16 groups of 16 columns behind one wait (r holds 32 or 64 registers)
+      auto fetch_tmem = [&](int col, auto& r, int n16) {
+        constexpr int W = sizeof(r) / sizeof(r[0]);
+#pragma unroll
+        for (int k = 0; k < W / 16; ++k)
+          if (k < n16) tmem_ld16(taddr_row + col + 16 * k, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * k]));
+        tmem_ld_wait_tied(r);
       };
       if (sg.ncontrib == 1 && p.push_mode == 0 && p.direct_epi) {
         direct_epilogue<EPI, TRANS>(p, s, fetch_tmem, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
@@ -971,24 +1078,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float* part_row = p.workspace + (size_t)(sg.sk_tile + sg.first_cta + 1) * tile_floats +
                                 (size_t)row * p.bn;
         const int nparts = sg.ncontrib - 1;
-        auto fetch_sum = [&](int col, uint32_t (&r)[16]) {
-          tmem_ld16(taddr_row + col, r);
-          float4 y[4];
-          float a[16];
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) a[i] = __uint_as_float(r[i]);
+        auto fetch_sum = [&](int col, auto& r, int n16) {
+          constexpr int W = sizeof(r) / sizeof(r[0]);
+          fetch_tmem(col, r, n16);
           for (int k = 0; k < nparts; ++k) {
             const float4* src = reinterpret_cast<const float4*>(part_row + (size_t)k * tile_floats + col);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) y[i] = __ldcg(src + i);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              a[4 * i] += y[i].x; a[4 * i + 1] += y[i].y; a[4 * i + 2] += y[i].z; a[4 * i + 3] += y[i].w;
+            for (int i = 0; i < W / 4; ++i) {
+              if (i < 4 * n16) {
+                const float4 y = __ldcg(src + i);
+                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + y.x);
+                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + y.y);
+                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + y.z);
+                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + y.w);
+              }
             }
           }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(a[i]);
         };
         direct_epilogue<EPI, TRANS>(p, s, fetch_sum, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
         if (trace && et == 0) trace[11] = globaltimer_ns();
@@ -1267,9 +1372,18 @@ static int kbox_for(bool trans) {
   return v > 0 ? v : (trans ? 2 : 1);
 }
 
-static SmemPlan smem_plan(int bn, int C, int kbox) {
+// epilogue region of the whole-tile path: swap-AB SiLU hands bf16 "up" rows across warps
+// ([2 blocks][2 directions][64][17] words) and stages its bf16 output ([64][64]); all of it fits
+// the staging slots
+static int epi_region_bytes(int epi, bool trans) {
+  return (trans && epi == EPI_SILU_BF16) ? std::max(EPI_STAGING_BYTES, (4 * 64 * 17) * 4 + 64 * 64 * 2)
+                                         : EPI_STAGING_BYTES;
+}
+
+static SmemPlan smem_plan(int bn, int C, int kbox, int epi, bool trans) {
   SmemPlan sp;
-  sp.epi_bytes = C > 1 ? std::max(EPI_STAGING_BYTES, ck_recv_bytes(bn, C)) : EPI_STAGING_BYTES;
+  const int base = epi_region_bytes(epi, trans);
+  sp.epi_bytes = C > 1 ? std::max(base, ck_recv_bytes(bn, C)) : base;
   sp.stages = max_stages();
   while (sp.stages > 2 && gemm_smem_bytes(sp.stages, bn, sp.epi_bytes, kbox) > SMEM_BUDGET) --sp.stages;
   sp.bytes = gemm_smem_bytes(sp.stages, bn, sp.epi_bytes, kbox);
@@ -1279,7 +1393,7 @@ static SmemPlan smem_plan(int bn, int C, int kbox) {
 static int pick_ck(int tiles, int kb, int num_sms, int epi, int bn, int kbox) {
   int C = std::min(16, std::min(kb, num_sms / std::max(tiles, 1)));
   for (; C >= 2; --C) {
-    const SmemPlan sp = smem_plan(bn, C, kbox);
+    const SmemPlan sp = smem_plan(bn, C, kbox, epi, true);
     if (sp.bytes <= SMEM_BUDGET && max_active_clusters_for(epi, true, C, sp.bytes) >= tiles) return C;
   }
   return 0;
@@ -1398,7 +1512,7 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   p.ck = pl.ck;
   TORCH_CHECK(mode != 3 || pl.ck >= 2, "gemm_tcgen05: cluster split-K requested but not possible for this shape");
   TORCH_CHECK(p.ck <= 1 || (trans && push.empty()), "gemm_tcgen05: cluster split-K needs swap-AB and no push");
-  const SmemPlan sp = smem_plan(bn, p.ck, kbox);
+  const SmemPlan sp = smem_plan(bn, p.ck, kbox, (int)epi, trans);
   TORCH_CHECK(sp.bytes <= SMEM_BUDGET, "gemm_tcgen05: shared memory plan exceeds the budget");
   const int stages = sp.stages;
   p.epi_bytes = sp.epi_bytes;
@@ -1465,7 +1579,7 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, boo
   int bn = gemm_pick_bn((int)N, (int)epi, trans);
   const int kbox = kbox_for(trans);
   Plan pl = make_plan((int)M, (int)N, (int)K, bn, num_sms_cached((int)device), 0, (int)epi, trans, false, kbox);
-  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, smem_plan(bn, pl.ck, kbox).stages, pl.grid, pl.dp_tiles, pl.sk_iters,
+  return {bn, (int64_t)pl.ws_floats, pl.sk_tiles, smem_plan(bn, pl.ck, kbox, (int)epi, trans).stages, pl.grid, pl.dp_tiles, pl.sk_iters,
           pl.ck};
 }
 

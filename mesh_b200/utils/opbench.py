@@ -111,6 +111,7 @@ def trace_gemms(cfg, s, T, modes=(0, 1)):
             plan = ops.ext().gemm_plan(N, T, K, epi, True, torch.cuda.current_device())
             print(json.dumps(dict(trace=name, mode=mode, plan=list(plan), ctas=len(t), start_max=mx(0), waited=med(1),
                                   first_data_med=med(3), mma_done_med=med(4), mma_done_max=mx(4),
+                                  epi_start_med=med(5), epi_fetched_med=med(12), epi_stored_med=med(13),
                                   epi_done_max=mx(6), exit_max=mx(7), contrib_n=len(contrib),
                                   contrib_partial_written=cm(contrib, 8), contrib_flag_set=cm(contrib, 9),
                                   owner_n=len(owner), owner_wait_done=cm(owner, 10),
