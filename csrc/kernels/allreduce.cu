@@ -315,11 +315,12 @@ __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   if (threadIdx.x == 0) s_epoch = a.epoch[b] + 1;
   __syncthreads();
   const uint32_t e = s_epoch;
-  if (MC) fence_proxy_alias();  // partials were written through the unicast alias
+  // No proxy fences around the multicast accesses: the partials were written by earlier kernels
+  // in stream order and the sys-scope release/acquire flags order them for every rank (the same
+  // contract as the multicast all-reduce kernels of torch symmetric memory).
   const bool ok = block_barrier(a, 0, e, &s_ok);
   if (threadIdx.x == 0) a.epoch[b] = e;
   if (!ok) return;
-  if (MC) fence_proxy_alias();
   if (tr) a.trace[1] = globaltimer_ns();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long gw = (long)b * (AR_THREADS / 32) + warp;
@@ -348,10 +349,8 @@ __global__ void __launch_bounds__(AR_THREADS) ar_norm_kernel(const ArArgs a) {
   }
   if (tr) a.trace[2] = globaltimer_ns();
   if (TWO_SHOT) {
-    if (MC) fence_proxy_alias();
     __threadfence_system();
     block_barrier(a, 1, e, &s_ok);
-    if (MC) fence_proxy_alias();  // readers use the unicast alias of what arrived by multicast
   }
   if (tr) a.trace[3] = globaltimer_ns();
 }
