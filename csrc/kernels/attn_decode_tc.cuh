@@ -77,7 +77,9 @@ __global__ void __launch_bounds__(160) attn_decode_tc_kernel(const __grid_consta
   const int seq = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = a.hkv * G;
-  griddep_wait();
+  // Sequence lengths and block tables are step inputs copied before the step's first kernel; only
+  // Q and the newest key/value (position L-1) come from the kernel just before this one. Pages that
+  // do not hold position L-1 are streamed before griddepcontrol.wait, overlapping that kernel.
   griddep_launch_dependents();
   const int L = a.seq_lens[seq];
   const int w0 = (a.window > 0 && L > a.window) ? L - a.window : 0;
@@ -95,14 +97,7 @@ __global__ void __launch_bounds__(160) attn_decode_tc_kernel(const __grid_consta
     }
     fence_mbar_init();
   }
-  // Q rows 0..G-1 (rows G..15 zero), bf16, padded stride
-  for (int i = threadIdx.x; i < 16 * (D / 8); i += blockDim.x) {
-    const int r = i / (D / 8), c = i - r * (D / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) v = *reinterpret_cast<const uint4*>(a.q + (long)seq * hq * D + (h * G + r) * D + c * 8);
-    *reinterpret_cast<uint4*>(q_s + r * DTC_Q_LD + c * 8) = v;
-  }
-  __syncthreads();
+  __syncthreads();  // barriers initialised
 
   const int* bt = a.block_tables + (long)seq * a.max_pages;
   if (warp == 4) {
@@ -111,11 +106,16 @@ __global__ void __launch_bounds__(160) attn_decode_tc_kernel(const __grid_consta
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const uint64_t pol = policy_evict_first();
+      bool waited = false;
       for (int i = 0; i < nst; ++i) {
         const int s = i % DTC_STAGES;
         const uint32_t ph = (i / DTC_STAGES) & 1;
         if (!mbar_wait_bounded(&empty[s], ph ^ 1, a.err, ERR_MBAR_TIMEOUT_PRODUCER, nullptr, DTC_WAIT_NS)) break;
         const int key0 = s0 + (st_begin + i) * DTC_KEYS;
+        if (!waited && key0 + DTC_KEYS > L - 1) {  // this stage holds the newest key/value
+          griddep_wait();
+          waited = true;
+        }
         const int npages = min(4, (L - key0 + 15) / 16);
         mbar_arrive_expect_tx(&full[s], (uint32_t)npages * 4 * DTC_BOX_BYTES);
         uint8_t* st = stages + s * DTC_STAGE_BYTES;
@@ -133,6 +133,15 @@ __global__ void __launch_bounds__(160) attn_decode_tc_kernel(const __grid_consta
     }
   } else {
     // ------------------------------- consumers -------------------------------
+    griddep_wait();  // Q comes from the RoPE kernel just before
+    // Q rows 0..G-1 (rows G..15 zero), bf16, padded stride
+    for (int i = threadIdx.x; i < 16 * (D / 8); i += 128) {
+      const int r = i / (D / 8), c = i - r * (D / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < G) v = *reinterpret_cast<const uint4*>(a.q + (long)seq * hq * D + (h * G + r) * D + c * 8);
+      *reinterpret_cast<uint4*>(q_s + r * DTC_Q_LD + c * 8) = v;
+    }
+    named_bar_sync(1, 128);
     // Q fragments (A operand, rows = heads), 8 k-steps of 16
     uint32_t qf[8][4];
     {
