@@ -39,7 +39,7 @@
 
 namespace mesh {
 
-enum EpiKind : int { EPI_STORE_BF16 = 0, EPI_STORE_F32 = 1, EPI_SILU_BF16 = 2, EPI_ARGMAX = 3 };
+enum EpiKind : int { EPI_STORE_BF16 = 0, EPI_STORE_F32 = 1, EPI_SILU_BF16 = 2, EPI_ARGMAX = 3, EPI_QKV_ROPE = 4 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -59,6 +59,16 @@ struct GemmParams {
   int epi_bytes;      // shared memory of the epilogue region (staging, or split-K receive buffers)
   int vec_out;        // output rows start 16-byte aligned: whole-tile epilogue may store 16 bytes at once
   int direct_epi;     // whole tiles go TMEM -> registers -> global (else staged through shared memory)
+  // EPI_QKV_ROPE (swap-AB qkv projection, one 128-row tile = one head of 128 dims): RoPE on q and k
+  // heads from cos/sin tables at each token's position, q heads to `out` [T, hq*128], k and v heads
+  // straight into the paged KV pool [pages, hkv, page_size, 128] at each token's slot (< 0: skip)
+  const int* rope_pos;
+  const long* rope_slot;
+  const float* rope_cos;
+  const float* rope_sin;
+  __nv_bfloat16* rope_k;
+  __nv_bfloat16* rope_v;
+  int rope_hq, rope_hkv, rope_ps;
   int kbox;           // 64-wide k boxes per pipeline stage (1 or 2); a k-block is 64 * kbox wide
   void* out;
   long ldo;
@@ -441,6 +451,42 @@ __device__ __forceinline__ void stage_flush_bf16(const GemmParams& p, uint32_t s
   named_bar_sync(1, 128);  // staging tile free for the next block
 }
 
+// One head's worth of rotated (q, k) or plain (v) token rows, staged [ncols][128] bf16, written to
+// the q output or the paged KV pool as 16-byte chunks (a token's 128 dims are 256 contiguous bytes
+// in both layouts).
+__device__ __forceinline__ void stage_flush_qkv(const GemmParams& p, uint32_t stage, int ncols, int n0, int hd,
+                                                int et) {
+  named_bar_sync(1, 128);
+  for (int k = et; k < ncols * 16; k += 128) {
+    const int j = k >> 4, c8 = (k & 15) * 8;
+    const int n = n0 + j;
+    if (n >= p.N) continue;
+    __nv_bfloat16* dst;
+    if (hd < p.rope_hq) {
+      dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (long)n * p.ldo + (long)hd * 128 + c8;
+    } else {
+      const long sl = p.rope_slot[n];
+      if (sl < 0) continue;
+      const long page = sl / p.rope_ps, off = sl - page * p.rope_ps;
+      const bool is_k = hd < p.rope_hq + p.rope_hkv;
+      const int kh = is_k ? hd - p.rope_hq : hd - p.rope_hq - p.rope_hkv;
+      dst = (is_k ? p.rope_k : p.rope_v) + ((page * p.rope_hkv + kh) * p.rope_ps + off) * 128 + c8;
+    }
+    *reinterpret_cast<uint4*>(dst) = lds_u4(stage + (uint32_t)(j * 128 + c8) * 2);
+  }
+  named_bar_sync(1, 128);
+}
+
+// Half-split RoPE of dim d (0..127) of one head at token position `pos`: x is this dim's value,
+// y the value of dim d ^ 64 (both already rounded to bf16, as an unfused bf16 qkv buffer would be).
+__device__ __forceinline__ float rope_rotate(const GemmParams& p, int d, int pos, float x, float y) {
+  const int i = d & 63;
+  const float c = p.rope_cos[(long)pos * 64 + i], sn = p.rope_sin[(long)pos * 64 + i];
+  return d < 64 ? x * c - y * sn : y * sn + x * c;
+}
+
+__device__ __forceinline__ float bf16_round(float v) { return bf2f(f2bf(v)); }
+
 // ----------------------------------------------------------------------------------------------
 // Whole-tile epilogue straight from TMEM to global memory (no shared-memory staging): each thread
 // owns one accumulator row (TMEM lane). Swap-AB: the row is an output feature and its columns are
@@ -595,6 +641,33 @@ __device__ __forceinline__ void direct_epilogue(const GemmParams& p, const Smem&
         const int n = tn * p.bn + c + et;
         if (n < p.N) reinterpret_cast<float2*>(p.out)[(long)tm * p.ldo + n] = make_float2(best, __int_as_float(bi));
       }
+    }
+  } else if constexpr (TRANS && EPI == EPI_QKV_ROPE) {
+    const uint32_t xs = smem_u32(xbuf);             // [64 tokens][128 dims] bf16, before RoPE
+    const uint32_t stg = xs + 64 * 128 * 2;         // [64 tokens][128 dims] bf16, rotated
+    const bool rot = tm < p.rope_hq + p.rope_hkv;  // q and k heads rotate, v heads pass through
+    for (int c = 0; c < p.bn; c += 64) {
+      const int n16 = min(4, (p.bn - c + 15) / 16);
+      uint32_t r[64];
+      fetch(c, r, n16);
+      release_if_last(c + 64);
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (j < 16 * n16) stage_put_bf16(xs, 128, j, row, __uint_as_float(r[j]));
+      named_bar_sync(1, 128);
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        if (j < 16 * n16) {
+          const int n = tn * p.bn + c + j;
+          float v = bf16_round(__uint_as_float(r[j]));
+          if (rot && n < p.N) {
+            const uint16_t y16 = lds_u16(xs + (uint32_t)(j * 128 + (row ^ 64)) * 2);
+            v = rope_rotate(p, row, p.rope_pos[n], v, bf2f(*reinterpret_cast<const __nv_bfloat16*>(&y16)));
+          }
+          stage_put_bf16(stg, 128, j, row, v);
+        }
+      }
+      stage_flush_qkv(p, stg, 16 * n16, tn * p.bn + c, tm, threadIdx.x - 64);
     }
   } else if constexpr (TRANS && EPI == EPI_STORE_BF16) {
     const uint32_t stg = smem_u32(xbuf);  // [64 tokens][128 features] bf16
@@ -799,6 +872,30 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
       }
       named_bar_sync(1, 128);
     }
+  } else if constexpr (EPI == EPI_QKV_ROPE) {
+    // this CTA's tokens of one head: row et and its RoPE partner row et ^ 64 are both summed here
+    const uint32_t stg = smem_u32(s.a);
+    const bool rot = tm < p.rope_hq + p.rope_hkv;
+    for (int c = c_lo; c < c_hi; c += 32) {
+      const int nv = min(8, (c_hi - c) >> 2);
+      float4 v[8], y[8];
+      sum_row(et, c, nv, v);
+      if (rot) sum_row(et ^ 64, c, nv, y);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= nv) break;
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        const float yy[4] = {y[j].x, y[j].y, y[j].z, y[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = tn * p.bn + c + 4 * j + e;
+          float o = bf16_round(vv[e]);
+          if (rot && n < p.N) o = rope_rotate(p, et, p.rope_pos[n], o, bf16_round(yy[e]));
+          stage_put_bf16(stg, BM, c - c_lo + 4 * j + e, et, o);
+        }
+      }
+    }
+    if (c_hi > c_lo) stage_flush_qkv(p, stg, c_hi - c_lo, tn * p.bn + c_lo, tm, et);
   } else if constexpr (EPI == EPI_STORE_BF16) {
     // staged [cpc tokens][128 features] bf16 in the idle operand ring, written as 16-byte chunks
     const uint32_t stg = smem_u32(s.a);
@@ -1330,6 +1427,7 @@ static int max_active_clusters_for(int epi, bool trans, int C, size_t smem) {
     case EPI_STORE_F32: return max_active_clusters<EPI_STORE_F32, true>(C, smem);
     case EPI_SILU_BF16: return max_active_clusters<EPI_SILU_BF16, true>(C, smem);
     case EPI_ARGMAX: return max_active_clusters<EPI_ARGMAX, true>(C, smem);
+    case EPI_QKV_ROPE: return max_active_clusters<EPI_QKV_ROPE, true>(C, smem);
     default: return 0;
   }
 }
@@ -1476,9 +1574,19 @@ static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode, 
 }
 
 // out = A @ B^T (normal) or out^T = A @ B^T (trans). Returns nothing; errors go to `err`.
-void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn_req,
-                  int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
-                  const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push) {
+struct RopeArgs {
+  const int* pos;
+  const long* slot;
+  const float* cos;
+  const float* sin;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  int hq, hkv, ps;
+};
+
+static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans,
+                      int64_t bn_req, int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                      const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push, const RopeArgs* rope) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm_tcgen05: tensors must be CUDA");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_tcgen05: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tcgen05: A [M,K], B [N,K]");
@@ -1533,7 +1641,19 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
   // Swap-AB CTAs that stream many tiles (LM head) keep the staged epilogue, whose cooperative
   // column-at-a-time stores measured faster there; latency-bound few-tile launches and the normal
   // orientation store straight from registers.
-  p.direct_epi = (!trans || pl.tiles <= 2 * pl.grid) ? 1 : 0;
+  p.direct_epi = (!trans || pl.tiles <= 2 * pl.grid || epi == EPI_QKV_ROPE) ? 1 : 0;
+  if (epi == EPI_QKV_ROPE) {
+    TORCH_CHECK(rope != nullptr && trans && push.empty(), "qkv+rope epilogue: swap-AB, no push");
+    p.rope_pos = rope->pos;
+    p.rope_slot = rope->slot;
+    p.rope_cos = rope->cos;
+    p.rope_sin = rope->sin;
+    p.rope_k = rope->k;
+    p.rope_v = rope->v;
+    p.rope_hq = rope->hq;
+    p.rope_hkv = rope->hkv;
+    p.rope_ps = rope->ps;
+  }
   // push = [mode, my_rank, world, rows, slot_stride, ldo, base_0 .. base_{world-1}]
   if (!push.empty()) {
     TORCH_CHECK(epi == EPI_STORE_BF16 && push.size() >= 6, "fused reduce-scatter needs the bf16 epilogue");
@@ -1567,9 +1687,53 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
     case EPI_SILU_BF16 * 2 + 0: launch_typed<EPI_SILU_BF16, false>(ta, tb, p, grid, smem, stream); break;
     case EPI_SILU_BF16 * 2 + 1: launch_typed<EPI_SILU_BF16, true>(ta, tb, p, grid, smem, stream); break;
     case EPI_ARGMAX * 2 + 1: launch_typed<EPI_ARGMAX, true>(ta, tb, p, grid, smem, stream); break;
+    case EPI_QKV_ROPE * 2 + 1: launch_typed<EPI_QKV_ROPE, true>(ta, tb, p, grid, smem, stream); break;
     default: TORCH_CHECK(false, "gemm_tcgen05: unknown epilogue ", epi);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans, int64_t bn_req,
+                  int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                  const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push) {
+  TORCH_CHECK(epi != EPI_QKV_ROPE, "gemm_tcgen05: use gemm_qkv_rope for the fused RoPE epilogue");
+  gemm_impl(A, B, out, epi, trans, bn_req, mode, workspace, counters, err, trace, push, nullptr);
+}
+
+// Decode qkv projection with RoPE and the paged KV write fused into the epilogue (swap-AB):
+// w [(hq + 2*hkv) * 128, H] rows = q heads, k heads, v heads; x [T, H]; q_out [T, hq*128];
+// kcache / vcache one layer of the pool [pages, hkv, page_size, 128]; pos int32 [T]; slot int64 [T]
+// (< 0: padding token, nothing written); cos / sin fp32 [max_pos, 64].
+void gemm_qkv_rope(const at::Tensor& w, const at::Tensor& x, at::Tensor& q_out, const at::Tensor& pos,
+                   const at::Tensor& slot, const at::Tensor& cos_t, const at::Tensor& sin_t, at::Tensor& kcache,
+                   at::Tensor& vcache, int64_t hq, int64_t hkv, int64_t mode, at::Tensor& workspace,
+                   at::Tensor& counters, at::Tensor& err) {
+  const int64_t T = x.size(0);
+  TORCH_CHECK(w.size(0) == (hq + 2 * hkv) * 128, "gemm_qkv_rope: head_dim 128, rows q|k|v");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.size(0) == T && q_out.size(1) == hq * 128 &&
+                  q_out.scalar_type() == at::kBFloat16,
+              "gemm_qkv_rope: q_out [T, hq*128] bf16 contiguous");
+  TORCH_CHECK(kcache.is_contiguous() && vcache.is_contiguous() && kcache.dim() == 4 && kcache.size(1) == hkv &&
+                  kcache.size(3) == 128 && vcache.sizes() == kcache.sizes() &&
+                  kcache.scalar_type() == at::kBFloat16 && vcache.scalar_type() == at::kBFloat16,
+              "gemm_qkv_rope: kv pages [pages, hkv, page_size, 128] bf16");
+  TORCH_CHECK(pos.is_cuda() && pos.numel() >= T && pos.scalar_type() == at::kInt && slot.is_cuda() &&
+                  slot.numel() >= T && slot.scalar_type() == at::kLong,
+              "gemm_qkv_rope: pos int32 [T], slot int64 [T] on the device");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat && cos_t.size(-1) == 64 &&
+                  sin_t.size(-1) == 64 && cos_t.is_contiguous() && sin_t.is_contiguous(),
+              "gemm_qkv_rope: cos/sin fp32 [max_pos, 64]");
+  RopeArgs r;
+  r.pos = pos.data_ptr<int>();
+  r.slot = reinterpret_cast<const long*>(slot.data_ptr<int64_t>());
+  r.cos = cos_t.data_ptr<float>();
+  r.sin = sin_t.data_ptr<float>();
+  r.k = reinterpret_cast<__nv_bfloat16*>(kcache.data_ptr());
+  r.v = reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr());
+  r.hq = (int)hq;
+  r.hkv = (int)hkv;
+  r.ps = (int)kcache.size(2);
+  gemm_impl(w, x, q_out, EPI_QKV_ROPE, true, 0, mode, workspace, counters, err, c10::nullopt, {}, &r);
 }
 
 // [bn, workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters, cluster split]

@@ -3,7 +3,8 @@
 Per layer (reference ``forward_layer``, ``agent/src/inference/forward_pass.rs:1946-2025``):
 
     qkv   = tcgen05 GEMM(normed, wqkv)                    (swap-AB for decode-sized T)
-    q     = RoPE(q); k,v -> paged KV pool                 (rope_kv_write)
+    q     = RoPE(q); k,v -> paged KV pool                 (decode: in the qkv GEMM epilogue;
+                                                          prefill: rope_kv_write)
     attn  = paged GQA attention                           (decode: split-KV; prefill: flash)
     part  = tcgen05 GEMM(attn, wo)                        -> own slot of the symmetric workspace
     resid, normed = AR(part) + resid, RMSNorm(mlp_norm)   (ar_fused_norm over NVLink; TP=1: add_rmsnorm)
@@ -167,8 +168,8 @@ class LlamaRunner:
         parity = 0
         for li, L in enumerate(w.layers):
             kc, vc = self.kv.k[li], self.kv.v[li]
-            ops.linear(normed, L.wqkv, out=qkv)
-            ops.rope_kv_write(qkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv)
+            ops.qkv_rope(normed, L.wqkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv,
+                         qkv_buf=qkv)
             if m.decode:
                 ops.attn_decode(q, kc, vc, m.block_tables, m.seq_lens, attn, self.scale, self.window,
                                 max_len_hint=m.max_q_len)

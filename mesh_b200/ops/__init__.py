@@ -6,6 +6,8 @@ holds plain fp32 PyTorch versions used only by tests as the numerical oracle.
 """
 from __future__ import annotations
 
+import os
+
 import math
 import threading
 from typing import Optional
@@ -149,6 +151,42 @@ def add_rmsnorm(resid: torch.Tensor, gamma: torch.Tensor, normed: torch.Tensor, 
     ext().add_rmsnorm(delta, resid, gamma, normed, eps)
     _count()
     return normed
+
+
+EPI_QKV_ROPE = 4
+# the fused decode qkv + RoPE + paged-KV-write GEMM; MESH_FUSED_QKV_ROPE=0 selects GEMM + rope_kv_write
+_FUSED_QKV_ROPE = os.environ.get("MESH_FUSED_QKV_ROPE", "1") != "0"
+
+
+def qkv_rope(x: torch.Tensor, wqkv: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, cos_t: torch.Tensor,
+             sin_t: torch.Tensor, q_out: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, hq: int,
+             hkv: int, qkv_buf: Optional[torch.Tensor] = None, mode: int = 0) -> torch.Tensor:
+    """q = RoPE(x @ wq.T); k = RoPE(x @ wk.T) and v = x @ wv.T written into the paged KV pool at
+    each token's slot. Decode-sized T with head_dim 128: one swap-AB GEMM whose epilogue applies
+    RoPE and writes q and the pages directly. Otherwise: GEMM into `qkv_buf`, then rope_kv_write."""
+    T = x.shape[0]
+    if T <= SWAP_AB_MAX_TOKENS and kcache.shape[-1] == 128 and (_FUSED_QKV_ROPE or mode != 0):
+        s = scratch(x.device)
+        M, K = wqkv.shape
+        if mode == 0:
+            key = (M, T, K, EPI_QKV_ROPE, True, x.device.index)
+            plan = _PLANS.get(key)
+            if plan is None:
+                plan = _PLANS[key] = ext().gemm_plan(M, T, K, EPI_QKV_ROPE, True, x.device.index)
+            if plan[2] > 0:
+                s.ensure_gemm(plan[1], plan[2])
+        else:
+            bn_ = ext().gemm_plan(M, T, K, EPI_QKV_ROPE, True, x.device.index)[0]
+            tiles = ((M + 127) // 128) * ((T + bn_ - 1) // bn_)
+            s.ensure_gemm((tiles + s.num_sms) * 128 * bn_, tiles)
+        ext().gemm_qkv_rope(wqkv, x, q_out, pos, slot, cos_t, sin_t, kcache, vcache, hq, hkv, mode, s.gemm_ws,
+                            s.gemm_counters, s.err)
+        _count()
+        return q_out
+    if qkv_buf is None:
+        qkv_buf = torch.empty(T, wqkv.shape[0], dtype=torch.bfloat16, device=x.device)
+    linear(x, wqkv, out=qkv_buf)
+    return rope_kv_write(qkv_buf, pos, slot, cos_t, sin_t, q_out, kcache, vcache, hq, hkv)
 
 
 def rope_kv_write(qkv, pos, slot, cos_t, sin_t, q_out, kcache, vcache, hq: int, hkv: int):

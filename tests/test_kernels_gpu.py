@@ -218,6 +218,42 @@ def test_rope_kv_write():
     assert kc[page_ids[0], :, 5].abs().sum() == 0  # slot -1 skipped
 
 
+@pytest.mark.parametrize("T,hq,hkv", [(40, 8, 2), (64, 32, 8), (64, 4, 1), (7, 8, 8)])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_qkv_rope_fused_matches_gemm_then_rope(T, hq, hkv, mode):
+    """Decode qkv GEMM with RoPE and the paged KV write in its epilogue == GEMM + rope_kv_write, for
+    every schedule (auto, whole tiles, stream-K, cluster split-K), including a padding slot (-1)."""
+    H, D, ps, pages = 1024, 128, 16, 12
+    if mode == 3 and ((hq + 2 * hkv) >= 148):
+        pytest.skip("cluster split-K needs fewer tiles than SMs")
+    x = _rand(T, H, seed=31)
+    w = _rand((hq + 2 * hkv) * D, H, std=0.05, seed=32)
+    pos = torch.arange(200, 200 + T, dtype=torch.int32, device=DEV)
+    page_ids = torch.tensor([3, 7, 1, 9, 11], device=DEV)
+    p = torch.arange(T, device=DEV)
+    slot = (page_ids[p // ps] * ps + p % ps).to(torch.int64)
+    slot[T // 2] = -1
+    cos, sin = ops.rope_tables(D, 5e5, 4096, DEV)
+    kc1 = torch.zeros(pages, hkv, ps, D, dtype=torch.bfloat16, device=DEV)
+    vc1, kc2, vc2 = torch.zeros_like(kc1), torch.zeros_like(kc1), torch.zeros_like(kc1)
+    q1 = torch.empty(T, hq * D, dtype=torch.bfloat16, device=DEV)
+    q2 = torch.empty_like(q1)
+    ops.qkv_rope(x, w, pos, slot, cos, sin, q1, kc1, vc1, hq, hkv, mode=mode if mode else 0)
+    qkv = torch.empty(T, w.shape[0], dtype=torch.bfloat16, device=DEV)
+    ops.linear(x, w, out=qkv)
+    ops.rope_kv_write(qkv, pos, slot, cos, sin, q2, kc2, vc2, hq, hkv)
+    torch.cuda.synchronize()
+    # against an fp32 reference of the whole op, and against the unfused kernels
+    y = x.float() @ w.float().T
+    qr = ref.rope(y[:, :hq * D], pos, D, 5e5)
+    assert rel_err(q1, qr) < 1e-2
+    assert rel_err(q1, q2) < 1e-2
+    assert rel_err(kc1, kc2) < 1e-2 and rel_err(vc1, vc2) < 1e-2
+    t = T // 2
+    pg, off = int(page_ids[t // ps]), t % ps
+    assert kc1[pg, :, off].abs().sum() == 0 and vc1[pg, :, off].abs().sum() == 0  # slot -1 skipped
+
+
 def test_embedding_and_argmax():
     V, H = 1000, 256
     table = _rand(V, H, seed=13)
