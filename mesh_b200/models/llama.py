@@ -18,6 +18,7 @@ computes full-vocab logits on every rank and samples on the host (forward_pass.r
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -27,6 +28,22 @@ import torch.distributed as dist
 from .. import ops
 from ..config import EngineConfig, ModelConfig
 from .weights import DeviceWeights
+
+
+# MESH_NVTX=1: host NVTX ranges per layer and for the LM head (for nsys/ncu timelines).
+# MESH_POISON=1: fill activation scratch with NaN before each step (catches unwritten outputs).
+_NVTX = os.environ.get("MESH_NVTX", "0") == "1"
+_POISON = os.environ.get("MESH_POISON", "0") == "1"
+
+
+def _nvtx_range(name):
+    """Open an NVTX range (name) or close the innermost one (None); no-op unless MESH_NVTX=1."""
+    if not _NVTX:
+        return
+    if name is None:
+        torch.cuda.nvtx.range_pop()
+    else:
+        torch.cuda.nvtx.range_push(name)
 
 
 class KVPool:
@@ -158,6 +175,7 @@ class LlamaRunner:
             return t
 
         resid, normed = self._resid_normed(T)
+        rng = _nvtx_range
         ops.embedding(m.ids, w.embedding, resid)
         ops.add_rmsnorm(resid, w.layers[0].attn_norm, normed, c.rms_norm_eps)
         qkv_w = (self.hq + 2 * self.hkv) * self.D
@@ -165,8 +183,14 @@ class LlamaRunner:
         q = buf("q", (T, self.hq * self.D))
         attn = buf("attn", (T, self.hq * self.D))
         h = buf("h", (T, w.i_pad))
+        if _POISON:
+            # debug: NaN in every activation scratch buffer, so a kernel that skips part of its
+            # output shows up as NaN in the result instead of reusing the previous step's values
+            for t in (qkv, q, attn, h):
+                t.fill_(float("nan"))
         parity = 0
         for li, L in enumerate(w.layers):
+            rng(f"layer {li}")
             kc, vc = self.kv.k[li], self.kv.v[li]
             ops.qkv_rope(normed, L.wqkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv,
                          qkv_buf=qkv)
@@ -186,7 +210,9 @@ class LlamaRunner:
             gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
             self._reduce(part, resid, normed, gamma, parity)
             parity ^= 1
+            rng(None)
 
+        rng("lm_head")
         if m.last_idx is not None:
             S = m.last_idx.shape[0]
             final = buf("final", (S, self.H))
@@ -209,4 +235,5 @@ class LlamaRunner:
             gathered = buf("cand_all", (self.world, S, 2), torch.float32)
             dist.all_gather_into_tensor(gathered.view(-1), cand.view(-1), group=self.group)
             ops.argmax_merge(gathered, ids_out)
+        rng(None)
         return ids_out

@@ -102,3 +102,18 @@ def test_engine_matches_oracle_greedy_first_token():
     out = eng.generate([prompt], 1)[0]
     want = int(np.argmax(LocalForwardPass(wref).prefill(prompt)))
     assert out[0] == want
+
+
+def test_poisoned_scratch_gives_same_tokens(monkeypatch):
+    """With every activation scratch buffer filled with NaN before each step, generation is
+    unchanged: each kernel writes all of the output it is responsible for."""
+    from mesh_b200.models import llama
+    cfg, wref, runner, dev = _setup()
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (9, 33)]
+    eng = Engine(runner, runner.ecfg, max_batch=8)
+    clean = eng.generate(prompts, 5)
+    monkeypatch.setattr(llama, "_POISON", True)
+    poisoned = eng.generate(prompts, 5)
+    eng.close()
+    assert poisoned == clean
