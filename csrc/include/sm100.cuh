@@ -325,6 +325,10 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 // ----------------------------------------------------------------------------------------------
 // system-scope flag access for cross-GPU synchronisation over NVLink peer memory
 // ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

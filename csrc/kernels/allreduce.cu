@@ -22,6 +22,7 @@
 #include <torch/extension.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "../include/sm100.cuh"
 #include "../include/launch.h"
@@ -51,7 +52,18 @@ struct ArArgs {
   // NVLS multicast base of the symmetric workspace (same offsets as base[]); 0 = plain peer loads
   uint64_t mc;
   uint64_t* trace;  // optional: block 0 records %globaltimer at start / after barrier / rows done / end
+  // 1: one sys-scope fence per block, then relaxed flag stores (instead of a release store per peer)
+  int single_fence;
 };
+
+inline int ar_single_fence() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MESH_AR_SINGLE_FENCE");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v;
+}
 
 __device__ __forceinline__ uint32_t* flag_ptr(const ArArgs& a, int peer, int phase, int block, int src) {
   return reinterpret_cast<uint32_t*>(a.base[peer] + a.off_flags) +
@@ -61,9 +73,17 @@ __device__ __forceinline__ uint32_t* flag_ptr(const ArArgs& a, int peer, int pha
 // Returns false (uniformly across the block) if a peer did not arrive in time.
 __device__ __forceinline__ bool block_barrier(const ArArgs& a, int phase, uint32_t e, int* s_ok) {
   const int b = blockIdx.x;
-  if (threadIdx.x == 0) *s_ok = 1;
+  if (threadIdx.x == 0) {
+    *s_ok = 1;
+    if (a.single_fence) fence_acq_rel_sys();
+  }
   __syncthreads();
-  if (threadIdx.x < a.world) st_release_sys(flag_ptr(a, threadIdx.x, phase, b, a.rank), e);
+  if (threadIdx.x < a.world) {
+    if (a.single_fence)
+      st_relaxed_sys(flag_ptr(a, threadIdx.x, phase, b, a.rank), e);
+    else
+      st_release_sys(flag_ptr(a, threadIdx.x, phase, b, a.rank), e);
+  }
   if (threadIdx.x < a.world) {
     if (!wait_flag_geq(flag_ptr(a, a.rank, phase, b, threadIdx.x), e, a.timeout_ns, a.err)) *s_ok = 0;
   }
@@ -374,7 +394,9 @@ inline void launch_ar_t(const ArArgs& a, bool two_shot, cudaStream_t st) {
   }
 }
 
-inline void launch_ar(const ArArgs& a, bool two_shot, cudaStream_t st) {
+inline void launch_ar(const ArArgs& a_in, bool two_shot, cudaStream_t st) {
+  ArArgs a = a_in;
+  a.single_fence = ar_single_fence();
   if (a.mc != 0 && !a.push)
     launch_ar_t<true>(a, two_shot, st);
   else
