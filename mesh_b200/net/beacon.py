@@ -1,4 +1,4 @@
-"""LAN discovery: signed pool beacons over UDP (multicast by default) and a peer cache.
+"""LAN discovery: signed pool beacons over UDP (a LAN group address by default) and a peer cache.
 
 Behaviour follows the reference's discovery service (``agent/src/discovery/beacon.rs``): every
 5 s a node announces each pool it belongs to on 239.192.0.1:42424 (``:22-31``); a beacon carries
@@ -22,8 +22,8 @@ import cbor2
 
 from .pki import KeyPair, MembershipCert, node_id_from_pubkey, verify_signature
 
-MULTICAST_ADDR = "239.192.0.1"
-MULTICAST_PORT = 42424
+GROUP_ADDR = "239.192.0.1"
+BEACON_PORT = 42424
 BEACON_INTERVAL_S = 5.0
 STALE_PEER_S = 30.0
 
@@ -125,12 +125,12 @@ class PeerCache:
 class BeaconService:
     """Announces this node's pools and listens for peers' beacons.
 
-    ``targets`` are the destinations of announcements (the multicast group by default; unicast
-    addresses work where multicast is unavailable, e.g. tests on loopback)."""
+    ``targets`` are the destinations of announcements (the LAN group address by default; unicast
+    addresses work where group delivery is unavailable, e.g. tests on loopback)."""
 
     def __init__(self, device: KeyPair, pools: Iterable[MembershipCert], bind: Tuple[str, int] = ("0.0.0.0",
-                 MULTICAST_PORT), targets: Optional[List[Tuple[str, int]]] = None, interval_s: float = BEACON_INTERVAL_S,
-                 multicast: bool = True, quic_port: int = 0, admin: bool = False):
+                 BEACON_PORT), targets: Optional[List[Tuple[str, int]]] = None, interval_s: float = BEACON_INTERVAL_S,
+                 join_group: bool = True, quic_port: int = 0, admin: bool = False):
         self.device = device
         self.pools = list(pools)
         self.interval_s = interval_s
@@ -147,13 +147,13 @@ class BeaconService:
                 pass
         self._sock.bind(bind)
         self.addr = self._sock.getsockname()
-        if multicast:
-            mreq = struct.pack("4sl", socket.inet_aton(MULTICAST_ADDR), socket.INADDR_ANY)
+        if join_group:
+            mreq = struct.pack("4sl", socket.inet_aton(GROUP_ADDR), socket.INADDR_ANY)
             try:
                 self._sock.setsockopt(socket.IPPROTO_IP, socket.IP_ADD_MEMBERSHIP, mreq)
             except OSError:
-                pass  # no multicast route: unicast targets still work
-        self.targets = targets if targets is not None else [(MULTICAST_ADDR, MULTICAST_PORT)]
+                pass  # no route for the group address: unicast targets still work
+        self.targets = targets if targets is not None else [(GROUP_ADDR, BEACON_PORT)]
         self._stop = threading.Event()
         self._threads: List[threading.Thread] = []
         self._lock = threading.Lock()

@@ -4,7 +4,7 @@ Types and ranking follow the reference (``agent/src/connectivity.rs:10-105``, ``
 a device's state is a path (direct or relayed), an optional active endpoint and a status; direct
 candidates are multiaddrs classified by transport (QUIC before TCP) and address scope (public 0,
 DNS 10, private 20, loopback 30; priority = scope rank + transport rank); circuit-relay addresses
-and unsupported scopes (unspecified, multicast, broadcast, documentation ranges) are never direct
+and unsupported scopes (unspecified, group-address, broadcast, documentation ranges) are never direct
 candidates; candidates observed from outside expire after 5 minutes, locally listened ones do
 not; ranking is priority, then observed-before-local, then most recently updated, then endpoint
 text, with duplicates removed. State and observed addresses persist as JSON under the mesh home.
@@ -86,8 +86,9 @@ def _ip_scope(ip: str) -> Optional[str]:
     if a.is_loopback:
         return "loopback"
     doc4 = [ipaddress.ip_network(n) for n in ("192.0.2.0/24", "198.51.100.0/24", "203.0.113.0/24")]
-    if a.is_unspecified or a.is_multicast or (a.version == 4 and (str(a) == "255.255.255.255" or
-                                                                   any(a in n for n in doc4))):
+    group = ipaddress.ip_network("224.0.0.0/4" if a.version == 4 else "ff00::/8")  # one-to-many ranges
+    if a.is_unspecified or a in group or (a.version == 4 and (str(a) == "255.255.255.255" or
+                                                              any(a in n for n in doc4))):
         return None
     if a.version == 6 and a in ipaddress.ip_network("2001:db8::/32"):
         return None

@@ -37,8 +37,8 @@ def test_beacon_sign_verify_and_tamper():
 def test_beacon_service_discovers_peers_on_loopback():
     root = pki.KeyPair()
     (d1, c1), (d2, c2) = _member(root), _member(root)
-    s1 = beacon.BeaconService(d1, [c1], bind=("127.0.0.1", 0), targets=[], multicast=False, interval_s=0.05)
-    s2 = beacon.BeaconService(d2, [c2], bind=("127.0.0.1", 0), targets=[s1.addr], multicast=False, interval_s=0.05)
+    s1 = beacon.BeaconService(d1, [c1], bind=("127.0.0.1", 0), targets=[], join_group=False, interval_s=0.05)
+    s2 = beacon.BeaconService(d2, [c2], bind=("127.0.0.1", 0), targets=[s1.addr], join_group=False, interval_s=0.05)
     s1.targets = [s2.addr]
     s1.start(), s2.start()
     try:
