@@ -284,31 +284,72 @@ def cmd_ledger(a):
 
 
 # ------------------------------------------------------------------------------------------ pool
+def _device_keypair():
+    """This device's ed25519 key (from `mesh device init`); a fresh key if the device is not initialised."""
+    from ..net import pki
+    try:
+        return pki.KeyPair.from_seed(bytes.fromhex(load_device()["private_key"]))
+    except SystemExit:
+        return pki.KeyPair()
+
+
 def cmd_pool(a):
+    """Pools (reference ``agent/src/pki``): a pool is an ed25519 root key; its id is derived from the
+    root public key; members hold certificates signed by the root; `peers --listen-seconds` runs LAN
+    beacon discovery for that long and records the verified peers."""
+    from ..net import beacon, pki
     pools = home() / "pools"
     pools.mkdir(exist_ok=True)
     if a.action == "create":
-        priv, pub = gen_keypair()
-        pid = str(uuid.uuid4())
-        (pools / f"{pid}.json").write_text(json.dumps({"pool_id": pid, "name": a.name, "root_public_key": pub,
-                                                       "root_private_key": priv, "role": "admin",
-                                                       "created_at": int(time.time())}, indent=2))
-        print(json.dumps({"pool_id": pid, "root_public_key": pub}))
+        root = pki.KeyPair()
+        dev = _device_keypair()
+        cert = pki.MembershipCert.issue(dev.public, root, pki.ROLE_ADMIN)
+        pid = root.pool_id.hex()
+        (pools / f"{pid}.json").write_text(json.dumps({
+            "pool_id": pid, "name": a.name, "root_public_key": root.public.hex(), "root_seed": root.seed().hex(),
+            "role": "admin", "cert": cert.to_dict(), "created_at": int(time.time())}, indent=2))
+        print(json.dumps({"pool_id": pid, "root_public_key": root.public.hex()}))
+    elif a.action == "issue":
+        p = json.loads((pools / f"{a.pool_id}.json").read_text())
+        if "root_seed" not in p:
+            raise SystemExit("only the pool admin (holder of the root key) can issue certificates")
+        root = pki.KeyPair.from_seed(bytes.fromhex(p["root_seed"]))
+        cert = pki.MembershipCert.issue(bytes.fromhex(a.device_pubkey), root,
+                                        pki.ROLE_ADMIN if a.admin else pki.ROLE_MEMBER)
+        print(json.dumps(cert.to_dict()))
     elif a.action == "join":
-        (pools / f"{a.pool_id}.json").write_text(json.dumps({"pool_id": a.pool_id, "name": a.name,
-                                                             "root_public_key": a.pool_root_pubkey, "role": "member",
-                                                             "joined_at": int(time.time())}, indent=2))
-        print(json.dumps({"pool_id": a.pool_id, "joined": True}))
+        entry = {"pool_id": a.pool_id, "name": a.name, "root_public_key": a.pool_root_pubkey, "role": "member",
+                 "joined_at": int(time.time())}
+        if pki.pool_id_from_pubkey(bytes.fromhex(a.pool_root_pubkey)).hex() != a.pool_id:
+            raise SystemExit("pool id does not match the pool root public key")
+        if a.cert:
+            cert = pki.MembershipCert.from_dict(json.loads(Path(a.cert).read_text()))
+            if not cert.verify(bytes.fromhex(a.pool_root_pubkey)):
+                raise SystemExit("membership certificate does not verify against the pool root key")
+            entry["cert"] = cert.to_dict()
+            entry["role"] = cert.role
+        (pools / f"{a.pool_id}.json").write_text(json.dumps(entry, indent=2))
+        print(json.dumps({"pool_id": a.pool_id, "joined": True, "certified": "cert" in entry}))
     elif a.action == "list":
         out = []
         for f in sorted(pools.glob("*.json")):
             p = json.loads(f.read_text())
-            p.pop("root_private_key", None)
+            p.pop("root_seed", None)
             out.append(p)
         print(json.dumps(out, indent=2))
     elif a.action == "peers":
         f = pools / f"{a.pool_id}.json"
-        print(json.dumps(json.loads(f.read_text()).get("peers", []) if f.exists() else []))
+        p = json.loads(f.read_text()) if f.exists() else {}
+        if a.listen_seconds > 0 and "cert" in p:
+            svc = beacon.BeaconService(_device_keypair(), [pki.MembershipCert.from_dict(p["cert"])],
+                                       admin=p.get("role") == "admin").start()
+            time.sleep(a.listen_seconds)
+            peers = svc.peers(bytes.fromhex(a.pool_id))
+            svc.close()
+            p["peers"] = [{"node_id": x.node_id.hex(), "addr": f"{x.addr[0]}:{x.addr[1]}", "quic_port": x.quic_port,
+                           "capabilities": x.capabilities, "last_seen": int(x.last_seen)} for x in peers]
+            f.write_text(json.dumps(p, indent=2))
+        print(json.dumps(p.get("peers", [])))
     else:
         print(json.dumps({"pools": len(list(pools.glob("*.json")))}))
 
@@ -431,10 +472,17 @@ def build_parser():
     pj.add_argument("--pool-id", required=True)
     pj.add_argument("--pool-root-pubkey", required=True)
     pj.add_argument("-n", "--name")
+    pj.add_argument("--cert", help="membership certificate (JSON) issued by the pool admin")
     pj.set_defaults(fn=cmd_pool)
     pool.add_parser("list").set_defaults(fn=cmd_pool)
     pp = pool.add_parser("peers")
     pp.add_argument("--pool-id", required=True)
+    pp.add_argument("--listen-seconds", type=float, default=0.0, help="run LAN beacon discovery this long")
+    pi = pool.add_parser("issue")
+    pi.add_argument("--pool-id", required=True)
+    pi.add_argument("--device-pubkey", required=True)
+    pi.add_argument("--admin", action="store_true")
+    pi.set_defaults(fn=cmd_pool)
     pp.set_defaults(fn=cmd_pool)
     pool.add_parser("status").set_defaults(fn=cmd_pool)
     doc = sub.add_parser("doctor")

@@ -71,3 +71,30 @@ def test_cli_doctor_preflight_runs(capsys):
     names = {c["check"] for c in out}
     assert {"python", "torch", "kernels_built", "runtime_built"} <= names
     assert rc in (0, 1)
+
+
+def test_cli_pool_certificates(tmp_path, monkeypatch, capsys):
+    """An admin creates a pool and issues a certificate; a second device joins with it, and a
+    certificate from another pool is refused."""
+    import json
+    from mesh_b200.cli import main as cli
+    from mesh_b200.net import pki
+    admin_home, member_home = tmp_path / "a", tmp_path / "m"
+    monkeypatch.setenv("MESHNET_HOME", str(admin_home))
+    assert cli.main(["pool", "create", "-n", "lab"]) == 0
+    created = json.loads(capsys.readouterr().out)
+    member = pki.KeyPair()
+    assert cli.main(["pool", "issue", "--pool-id", created["pool_id"], "--device-pubkey", member.public.hex()]) == 0
+    cert_file = tmp_path / "cert.json"
+    cert_file.write_text(capsys.readouterr().out)
+    monkeypatch.setenv("MESHNET_HOME", str(member_home))
+    assert cli.main(["pool", "join", "--pool-id", created["pool_id"], "--pool-root-pubkey",
+                     created["root_public_key"], "--cert", str(cert_file)]) == 0
+    assert json.loads(capsys.readouterr().out)["certified"] is True
+    other = pki.MembershipCert.issue(member.public, pki.KeyPair())
+    bad = tmp_path / "bad.json"
+    bad.write_text(json.dumps(other.to_dict()))
+    import pytest
+    with pytest.raises(SystemExit):
+        cli.main(["pool", "join", "--pool-id", created["pool_id"], "--pool-root-pubkey", created["root_public_key"],
+                  "--cert", str(bad)])
