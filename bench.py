@@ -40,7 +40,8 @@ def parse():
     ap.add_argument("--prefill-chunk", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the metric)")
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--nvls", action="store_true", help="fused all-reduce through NVSwitch multicast (multimem)")
+    ap.add_argument("--no-nvls", action="store_true",
+                    help="keep the fused all-reduce on plain peer loads (no NVSwitch multimem) at every TP degree")
     ap.add_argument("--ar-impl", default="auto",
                     choices=["auto", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
                     help="TP all-reduce: peer-memory pull (one/two-shot), fused GEMM->reduce-scatter push, or NCCL")
@@ -132,7 +133,7 @@ def main():
     max_seq = (P + G + 15) // 16 * 16
     ecfg = EngineConfig(tp=world, max_seq_len=max_seq, prefill_chunk_tokens=args.prefill_chunk,
                         use_cuda_graphs=not args.no_graphs, max_decode_batch_size=S,
-                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl, nvls=args.nvls)
+                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl, nvls=not args.no_nvls)
     w = synthetic_device_weights(cfg, rank, world, seed=1234, device=dev)
     pages = S * (max_seq // 16) + 64
     kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
@@ -212,7 +213,7 @@ def main():
                        "global_batch": S, "seq_len": P, "gen_tokens": G, "kv_page_tokens": 16,
                        "parallelism": f"tp{world}", "prefill_chunk_tokens": args.prefill_chunk,
                        "cuda_graphs": not args.no_graphs, "allreduce": args.ar_impl if args.impl != "nccl" else "nccl",
-                       "nvls": bool(args.nvls),
+                       "nvls": (not args.no_nvls) and world >= 8,
                        "l2": "inputs larger than L2 (weights %.1f GB per rank re-read every step)" % (w.nbytes() / 1e9)},
             "e2e": {"value": round(e2e, 1), "unit": "generated tokens/s through Engine.submit/run incl. prefill, "
                     "prompt H2D and token D2H", "h2d_bytes_per_step": S * P * 4 + S * 8 * 3,

@@ -142,7 +142,8 @@ class LlamaRunner:
         elif self.push_rs:
             self.symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
         elif self.use_fused_ar:
-            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
+            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T),
+                                           multicast=self.world >= 8)
         else:  # NCCL baseline
             dist.all_reduce(part, group=self.group)
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
