@@ -1,6 +1,6 @@
 """Headline benchmark: decode tokens/s and p50 TTFT of the Llama-3-8B-shaped decoder, tensor
-parallel over N B200s of one node (BASELINE.json config #2: 64 concurrent sessions, 512-token
-uniform-random prompts, 128 greedy decode tokens, 16-token KV pages, continuous batching).
+parallel over N B200s of one node (the headline serving configuration: 64 concurrent sessions,
+512-token uniform-random prompts, 128 greedy decode tokens, 16-token KV pages, continuous batching).
 
 One bench "step" = one serving episode: submit 64 prompts, prefill them (chunked), decode 128
 tokens per session, read the generated tokens back to the host. Timing: CUDA events on the
@@ -10,6 +10,10 @@ of the named architecture; prompts are synthetic.
 
     python bench.py [--gpus N --steps K --warmup W]        # N>1: launch under torch.distributed.run
     python bench.py --impl reference                       # the reference arm
+    python bench.py --impl torch                           # plain PyTorch arm (cuBLAS + SDPA + NCCL)
+
+``--impl torch`` runs the same engine, episode and timing with ``baselines.torch_tp.TorchTPRunner``
+in place of the sm_100a runner: the comparison arm built from library code only.
 """
 from __future__ import annotations
 
@@ -24,7 +28,10 @@ import time
 import torch
 
 BASELINE_METRIC = "decode tokens/s + p50 TTFT, Llama-3 8B/70B TP at 1/2/4/8 B200, max over ranks"
-BASELINE_VALUE = None  # BASELINE.md publishes no number
+# The reference publishes no throughput figure. The comparison number per GPU count is the plain
+# PyTorch arm (``--impl torch``: cuBLAS linears, SDPA over gathered pages, NCCL all-reduce) measured
+# with this script on the same B200 pool; None where it has not been measured.
+BASELINE_VALUE = {}
 
 
 def parse():
@@ -32,7 +39,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="mesh", choices=["mesh", "reference", "nccl"])
+    ap.add_argument("--impl", default="mesh", choices=["mesh", "reference", "nccl", "torch"])
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--sessions", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=512)
@@ -137,8 +144,12 @@ def main():
     w = synthetic_device_weights(cfg, rank, world, seed=1234, device=dev)
     pages = S * (max_seq // 16) + 64
     kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
-    runner = LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD if world > 1 else None,
-                         max_tokens=max(args.prefill_chunk + P, S))
+    grp = dist.group.WORLD if world > 1 else None
+    if args.impl == "torch":
+        from mesh_b200.baselines.torch_tp import TorchTPRunner
+        runner = TorchTPRunner(w, ecfg, kv, dev, group=grp, max_tokens=max(args.prefill_chunk + P, S))
+    else:
+        runner = LlamaRunner(w, ecfg, kv, dev, group=grp, max_tokens=max(args.prefill_chunk + P, S))
     eng = Engine(runner, ecfg, max_batch=S)
     g = torch.Generator().manual_seed(4321)
     prompts_host = torch.randint(0, cfg.vocab_size, (S, P), generator=g, dtype=torch.int32).pin_memory()
@@ -202,7 +213,9 @@ def main():
         line = {
             "metric": BASELINE_METRIC, "value": round(value, 1), "unit": "decode tokens/s (aggregate over ranks)",
             "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(total_ms / K, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": (round(value / BASELINE_VALUE[world], 3) if BASELINE_VALUE.get(world) else None),
+            "dtype": "bf16",
             "data": "synthetic: uniform-random prompt token ids, N(0,0.02) random-init weights",
             "impl": args.impl,
             "p50_ttft_ms": round(p50_ttft, 3), "prefill_ms_per_step": round(prefill_ms / K, 3),
@@ -212,8 +225,8 @@ def main():
             "config": {"model": args.model + ("" if not args.layers else f"-L{args.layers}-INVALID"),
                        "global_batch": S, "seq_len": P, "gen_tokens": G, "kv_page_tokens": 16,
                        "parallelism": f"tp{world}", "prefill_chunk_tokens": args.prefill_chunk,
-                       "cuda_graphs": not args.no_graphs, "allreduce": args.ar_impl if args.impl != "nccl" else "nccl",
-                       "nvls": (not args.no_nvls) and world >= 8,
+                       "cuda_graphs": not args.no_graphs, "allreduce": "nccl" if args.impl in ("nccl", "torch") else args.ar_impl,
+                       "nvls": (not args.no_nvls) and world >= 8 and args.impl == "mesh",
                        "l2": "inputs larger than L2 (weights %.1f GB per rank re-read every step)" % (w.nbytes() / 1e9)},
             "e2e": {"value": round(e2e, 1), "unit": "generated tokens/s through Engine.submit/run incl. prefill, "
                     "prompt H2D and token D2H", "h2d_bytes_per_step": S * P * 4 + S * 8 * 3,

@@ -78,7 +78,9 @@ extern "C" __attribute__((visibility("default"))) int mesh_attn_decode_noalloc(
   a.splits = splits;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.window = window;
-  mesh::launch_attn_decode(a, B, G, head_dim, static_cast<cudaStream_t>(stream));
-  if (cudaGetLastError() != cudaSuccess) return MESH_NOALLOC_ERR_LAUNCH;
+  // Only this call's own launches are checked (their return codes); an error that some earlier,
+  // unrelated launch left pending is neither reported as this call's failure nor cleared here.
+  if (mesh::launch_attn_decode(a, B, G, head_dim, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MESH_NOALLOC_ERR_LAUNCH;
   return MESH_NOALLOC_OK;
 }

@@ -58,8 +58,8 @@ void attn_decode(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor
   a.splits = (int)splits;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.window = (int)window;
-  launch_attn_decode(a, B, G, D, at::cuda::getCurrentCUDAStream());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const cudaError_t e = launch_attn_decode(a, B, G, D, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == cudaSuccess, "attn_decode launch failed: ", cudaGetErrorString(e));
 }
 
 // TMA-streamed tensor-core variant (head_dim 128, 16-token pages).

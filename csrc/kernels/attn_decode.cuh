@@ -191,30 +191,29 @@ __global__ void attn_decode_combine_kernel(const float* __restrict__ ws, __nv_bf
   }
 }
 
+// Returns the first launch error; the combine kernel is not enqueued when the split kernel failed
+// to launch (it would read scratch that nothing wrote).
 template <int G, int D>
-inline void launch_attn_decode_gd(const DecodeArgs& a, int B, cudaStream_t st) {
+inline cudaError_t launch_attn_decode_gd(const DecodeArgs& a, int B, cudaStream_t st) {
   dim3 grid(B, a.hkv, a.splits);
-  launch_k(attn_decode_kernel<G, D>, grid, dim3(DEC_WARPS * 32), 0, st, a);
-  if (a.splits > 1)
-    launch_k(attn_decode_combine_kernel<D>, dim3(B, a.hkv * G), dim3(D), 0, st, (const float*)a.ws, a.out,
-             a.hkv * G, a.splits);
+  cudaError_t e = launch_k(attn_decode_kernel<G, D>, grid, dim3(DEC_WARPS * 32), 0, st, a);
+  if (e != cudaSuccess || a.splits <= 1) return e;
+  return launch_k(attn_decode_combine_kernel<D>, dim3(B, a.hkv * G), dim3(D), 0, st, (const float*)a.ws, a.out,
+                  a.hkv * G, a.splits);
 }
 
 template <int D>
-inline void launch_attn_decode_d(const DecodeArgs& a, int B, int G, cudaStream_t st) {
+inline cudaError_t launch_attn_decode_d(const DecodeArgs& a, int B, int G, cudaStream_t st) {
   switch (G) {
-    case 1: launch_attn_decode_gd<1, D>(a, B, st); break;
-    case 2: launch_attn_decode_gd<2, D>(a, B, st); break;
-    case 4: launch_attn_decode_gd<4, D>(a, B, st); break;
-    default: launch_attn_decode_gd<8, D>(a, B, st); break;
+    case 1: return launch_attn_decode_gd<1, D>(a, B, st);
+    case 2: return launch_attn_decode_gd<2, D>(a, B, st);
+    case 4: return launch_attn_decode_gd<4, D>(a, B, st);
+    default: return launch_attn_decode_gd<8, D>(a, B, st);
   }
 }
 
-inline void launch_attn_decode(const DecodeArgs& a, int B, int G, int D, cudaStream_t st) {
-  if (D == 128)
-    launch_attn_decode_d<128>(a, B, G, st);
-  else
-    launch_attn_decode_d<64>(a, B, G, st);
+inline cudaError_t launch_attn_decode(const DecodeArgs& a, int B, int G, int D, cudaStream_t st) {
+  return D == 128 ? launch_attn_decode_d<128>(a, B, G, st) : launch_attn_decode_d<64>(a, B, G, st);
 }
 
 }  // namespace mesh

@@ -1,9 +1,9 @@
-"""Benchmarks of the BASELINE configurations other than the headline (``bench.py`` runs config #2).
+"""Benchmarks of the measured configurations other than the headline serving run (``bench.py``).
 
-    python -m mesh_b200.benchmarks cpu-tp2            # config #1: TinyLlama, cpu, TP=2 over loopback
-    torchrun ... -m mesh_b200.benchmarks prefill      # config #3: 2k/8k/32k single-sequence prefill (TTFT)
-    torchrun ... -m mesh_b200.benchmarks allreduce    # config #5: fused AR+norm vs NCCL vs host ring
-    torchrun ... -m mesh_b200.benchmarks serve70b     # config #4: 70B TP=8, 256 sessions, 10% KV handoff
+    python -m mesh_b200.benchmarks cpu-tp2            # TinyLlama shape, cpu, TP=2 over loopback
+    torchrun ... -m mesh_b200.benchmarks prefill      # 2k/8k/32k single-sequence prefill (TTFT)
+    torchrun ... -m mesh_b200.benchmarks allreduce    # fused AR+norm vs NCCL vs host ring
+    torchrun ... -m mesh_b200.benchmarks serve70b     # 70B TP=8, 256 sessions, 10% KV handoff
 
 Every GPU number is timed with CUDA events on the launching stream after warm-up and reported as
 the max over ranks; rank 0 prints one JSON line per measurement.
@@ -19,7 +19,7 @@ import time
 import numpy as np
 
 
-# ------------------------------------------------------------------------------------------ config 1
+# ------------------------------------------------------------------------------------------ cpu TP=2
 def _cpu_rank(rank, ports, out_q, prompt, gen, seed):
     from .config import get_preset
     from .models.sharding import shard_layout
@@ -98,7 +98,7 @@ def _max_over_ranks(x, dist, torch, dev):
     return float(t.item())
 
 
-# ------------------------------------------------------------------------------------------ config 3
+# ------------------------------------------------------------------------------------ prefill sweep
 def prefill(args):
     di, dist, torch = _dist()
     from .config import EngineConfig, get_preset
@@ -152,7 +152,7 @@ def prefill(args):
     mdist.shutdown()
 
 
-# ------------------------------------------------------------------------------------------ config 5
+# ------------------------------------------------------------------------------------ all-reduce sweep
 def allreduce(args):
     """Per-call device time of the fused all-reduce + residual + RMSNorm (plain peer loads and NVLS
     multicast, one-shot and two-shot) against NCCL all-reduce + the same norm kernel, each captured
@@ -270,7 +270,7 @@ def allreduce(args):
     mdist.shutdown()
 
 
-# ------------------------------------------------------------------------------------------ config 4
+# ------------------------------------------------------------------------------------ 70B serving
 def serve70b(args):
     """256 sessions, prompts U[128,2048], 256 output tokens; after half the decode steps 10% of
     the sessions are handed off (KV snapshot out, session released, snapshot re-imported as a new

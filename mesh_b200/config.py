@@ -93,11 +93,11 @@ class ModelConfig:
 
 
 PRESETS = {
-    # BASELINE config #1
+    # TinyLlama-1.1B shape (the CPU TP=2 loopback configuration)
     "tinyllama-1.1b": ModelConfig(2048, 32, 4, 22, 32000, 5632, 1e-5, 1e4, "tinyllama-1.1b"),
-    # BASELINE configs #2/#3
+    # Llama-3-8B shape (headline serving configuration and the prefill sweep)
     "llama3-8b": ModelConfig(4096, 32, 8, 32, 128256, 14336, 1e-5, 5e5, "llama3-8b"),
-    # BASELINE config #4
+    # Llama-3-70B shape (TP=8 serving with mid-run KV handoff)
     "llama3-70b": ModelConfig(8192, 64, 8, 80, 128256, 28672, 1e-5, 5e5, "llama3-70b"),
     # reference default ModelConfig (forward_pass.rs:174-186)
     "reference-default": ModelConfig(8192, 64, 8, 80, 32000, 28672, 1e-5, 1e4, "reference-default"),

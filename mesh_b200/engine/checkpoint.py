@@ -1,7 +1,8 @@
 """Checkpoint manager: CBOR checkpoints per job with hash, retention and recovery lookup.
 
 Restates ``agent/src/checkpoint/manager.rs:24-345`` and ``checkpoint/types.rs``: checkpoints live
-at ``<checkpoint_dir>/<job_id>/<checkpoint_id>.cbor``; retention keeps at most 5 per job, 10 GB in
+at ``<checkpoint_dir>/<job_id>/<checkpoint_id>.ckpt`` (the file name the reference uses,
+``manager.rs:155``, ``:251``, so either side finds the other's checkpoints); retention keeps at most 5 per job, 10 GB in
 total and 24 h of age (``types.rs:35-50``); every checkpoint carries a SHA-256 of its payload that
 is verified on load.
 """
@@ -17,6 +18,9 @@ from pathlib import Path
 from typing import List, Optional
 
 import cbor2
+
+# checkpoint file suffix; writes go to "<id>.ckpt.tmp" first and are renamed into place
+CKPT_SUFFIX = ".ckpt"
 
 
 def default_checkpoint_dir() -> Path:
@@ -102,8 +106,8 @@ class CheckpointManager:
         data = cp.to_bytes()
         d = self._job_dir(cp.metadata.job_id)
         d.mkdir(parents=True, exist_ok=True)
-        p = d / f"{cp.metadata.checkpoint_id}.cbor"
-        tmp = p.with_suffix(".tmp")
+        p = d / f"{cp.metadata.checkpoint_id}{CKPT_SUFFIX}"
+        tmp = d / f"{cp.metadata.checkpoint_id}{CKPT_SUFFIX}.tmp"
         tmp.write_bytes(data)
         tmp.replace(p)
         self.enforce_retention(cp.metadata.job_id)
@@ -113,7 +117,7 @@ class CheckpointManager:
         d = self._job_dir(job_id)
         out = []
         if d.exists():
-            for f in d.glob("*.cbor"):
+            for f in d.glob(f"*{CKPT_SUFFIX}"):
                 try:
                     out.append(CheckpointMetadata(**cbor2.loads(f.read_bytes())["metadata"]))
                 except Exception:
@@ -128,7 +132,7 @@ class CheckpointManager:
         m = metas[-1] if checkpoint_id is None else next((x for x in metas if x.checkpoint_id == checkpoint_id), None)
         if m is None:
             return None
-        return Checkpoint.from_bytes((self._job_dir(job_id) / f"{m.checkpoint_id}.cbor").read_bytes())
+        return Checkpoint.from_bytes((self._job_dir(job_id) / f"{m.checkpoint_id}{CKPT_SUFFIX}").read_bytes())
 
     def delete_job(self, job_id: str) -> None:
         shutil.rmtree(self._job_dir(job_id), ignore_errors=True)
@@ -143,14 +147,14 @@ class CheckpointManager:
             metas = self.list(j)
             for m in metas[:-self.config.max_checkpoints_per_job] if len(metas) > self.config.max_checkpoints_per_job \
                     else []:
-                (self._job_dir(j) / f"{m.checkpoint_id}.cbor").unlink(missing_ok=True)
+                (self._job_dir(j) / f"{m.checkpoint_id}{CKPT_SUFFIX}").unlink(missing_ok=True)
                 removed += 1
-        files = sorted(root.glob("*/*.cbor"), key=lambda f: f.stat().st_mtime)
+        files = sorted(root.glob(f"*/*{CKPT_SUFFIX}"), key=lambda f: f.stat().st_mtime)
         for f in files:
             if now - f.stat().st_mtime > self.config.retention_period_s:
                 f.unlink(missing_ok=True)
                 removed += 1
-        files = sorted(root.glob("*/*.cbor"), key=lambda f: f.stat().st_mtime)
+        files = sorted(root.glob(f"*/*{CKPT_SUFFIX}"), key=lambda f: f.stat().st_mtime)
         total = sum(f.stat().st_size for f in files)
         for f in files:
             if total <= self.config.max_total_storage_bytes:

@@ -223,12 +223,28 @@ def test_checkpoint_manager_retention_and_hash(tmp_path):
     assert [m.token_index for m in metas] == [2, 3]
     cp = cm.load("job")
     assert cp.generated_tokens == [1, 2, 3]
-    raw = bytearray((tmp_path / "job" / f"{cp.metadata.checkpoint_id}.cbor").read_bytes())
+    raw = bytearray((tmp_path / "job" / f"{cp.metadata.checkpoint_id}.ckpt").read_bytes())
     import cbor2
     d = cbor2.loads(bytes(raw))
     d["generated_tokens"] = [9, 9, 9]
     with pytest.raises(ValueError):
         Checkpoint.from_bytes(cbor2.dumps(d))
+
+
+def test_checkpoint_manager_reads_reference_named_files(tmp_path):
+    """A checkpoint written the reference's way (``<job>/<id>.ckpt``) is listed and loaded, and a
+    leftover temp file of an interrupted write is ignored."""
+    cm = CheckpointManager(CheckpointConfig(checkpoint_dir=tmp_path))
+    cp = Checkpoint.new("job-r", 7, {"prompt": "x"}, [5, 6], {"max_tokens": 8})
+    (tmp_path / "job-r").mkdir()
+    (tmp_path / "job-r" / f"{cp.metadata.checkpoint_id}.ckpt").write_bytes(cp.to_bytes())
+    (tmp_path / "job-r" / "partial.ckpt.tmp").write_bytes(b"garbage")
+    metas = cm.list("job-r")
+    assert [m.checkpoint_id for m in metas] == [cp.metadata.checkpoint_id]
+    got = cm.load("job-r")
+    assert got.generated_tokens == [5, 6] and got.metadata.token_index == 7
+    saved = cm.save(Checkpoint.new("job-r", 9, {}, [5, 6, 7], {}))
+    assert saved.suffix == ".ckpt" and not list((tmp_path / "job-r").glob("*.cbor"))
 
 
 def test_stats_keys_and_persist(tmp_path):
