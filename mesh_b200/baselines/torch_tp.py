@@ -5,10 +5,10 @@ This is the comparison arm for the sm_100a kernels, built only from library code
 * linears are ``torch.nn.functional.linear`` (cuBLAS/cuBLASLt);
 * RMSNorm is ``torch.nn.functional.rms_norm``; RoPE, SiLU and the residual adds are torch ops;
 * the paged KV pool is written with index assignment and read back by gathering each sequence's
-  pages into a contiguous [B, kv_heads, S, D] tensor, then ``scaled_dot_product_attention`` with a
-  length (and causal) mask. This is the shape of the reference's own attention path, which
-  concatenates its pages and applies an explicit mask every step (``forward_pass.rs:633-680``,
-  ``:2811-2835``);
+  pages into a contiguous [B, kv_heads, S, D] tensor; decode attention is two batched matmuls with
+  a masked fp32 softmax between them, prefill uses ``scaled_dot_product_attention`` (causal).
+  This is the shape of the reference's own attention path, which concatenates its pages and
+  applies an explicit mask every step (``forward_pass.rs:633-680``, ``:2811-2835``);
 * the two per-layer tensor-parallel reductions are ``torch.distributed.all_reduce`` (NCCL), as in
   the reference's forward layer (``forward_pass.rs:1974-2010``) but over NVLink instead of TCP;
 * the LM head is vocab-parallel; the greedy token is each rank's ``max`` merged through an NCCL
@@ -80,10 +80,14 @@ class TorchTPRunner:
         vc[page, :, off] = v
 
     def _attn_decode(self, q, kc, vc, m: StepMeta):
+        """Gather each sequence's pages, then grouped-query attention as two batched matmuls (the q
+        heads of one KV head form the rows of one [G, S] score block, so K/V are not repeated per
+        q head) with an fp32 masked softmax between them."""
         B = q.shape[0]
         bt = m.block_tables.long()
         ps = self.kv.page_size
         S = bt.shape[1] * ps
+        G = self.hq // self.hkv
         K = kc[bt].permute(0, 2, 1, 3, 4).reshape(B, self.hkv, S, self.D)
         V = vc[bt].permute(0, 2, 1, 3, 4).reshape(B, self.hkv, S, self.D)
         kpos = torch.arange(S, device=q.device)
@@ -91,9 +95,10 @@ class TorchTPRunner:
         mask = kpos[None, :] < lens
         if self.window > 0:
             mask &= kpos[None, :] >= lens - self.window
-        o = F.scaled_dot_product_attention(q.view(B, self.hq, 1, self.D), K, V, attn_mask=mask[:, None, None, :],
-                                           scale=self.scale, enable_gqa=True)
-        return o.reshape(B, self.hq * self.D)
+        sc = torch.matmul(q.view(B, self.hkv, G, self.D), K.transpose(-1, -2)).float() * self.scale
+        sc = sc.masked_fill(~mask[:, None, None, :], float("-inf"))
+        pr = torch.softmax(sc, -1).to(q.dtype)
+        return torch.matmul(pr, V).reshape(B, self.hq * self.D)
 
     def _attn_prefill(self, q, kc, vc, m: StepMeta):
         T = q.shape[0]
