@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--no-nvls", action="store_true",
                     help="keep the fused all-reduce on plain peer loads (no NVSwitch multimem) at every TP degree")
     ap.add_argument("--ar-impl", default="auto",
-                    choices=["auto", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
-                    help="TP all-reduce: peer-memory pull (one/two-shot), fused GEMM->reduce-scatter push, or NCCL")
+                    choices=["auto", "unfused", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
+                    help="TP all-reduce: auto (decode: fused into the o_proj/down GEMM launch), unfused (separate "
+                         "peer-memory kernel), pull one/two-shot, GEMM->reduce-scatter push, or NCCL")
     return ap.parse_args()
 
 

@@ -349,6 +349,16 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Arrival counter between the CTAs of one grid: returns the value before the add. acq_rel at gpu
+// scope, so the arriving CTA's earlier writes are visible to whichever CTA observes the final count.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 // Wait until *p == target for at most limit_ns (intra-GPU producer/consumer between CTAs).
 __device__ __forceinline__ bool wait_counter_eq(const int* p, int target, uint64_t limit_ns, int* err, int code) {
   if (ld_acquire_gpu(p) == target) return true;

@@ -49,6 +49,28 @@ constexpr int EPI_SLOT_FLOATS = BM * EPI_LD;
 constexpr int NUM_THREADS = 192;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: far above any legal wait
 
+// Fused tensor-parallel all-reduce tail of a decode o_proj / down_proj GEMM (swap-AB, bf16 out).
+// The epilogue pushes each token row of the partial product to the rank that owns the row (a
+// near-equal split of the T rows over the ranks) over NVLink; the tail then reduces the owned rows
+// over the ranks' pushed partials, adds the residual, applies RMSNorm and writes the normed rows
+// into every rank (NVLS multicast store, or one peer store per rank), all inside the same launch.
+constexpr int AR_TAIL_MAX_RANKS = 8;
+struct ArTail {
+  int on;
+  int rank, world, T, H, t_max;
+  unsigned long long ws[AR_TAIL_MAX_RANKS];  // symmetric workspace base of every rank (as mapped here)
+  unsigned long long mc;                     // multicast base of the workspace (0: plain peer stores)
+  long off_flags;    // uint32 [2 phases][AR_TAIL_MAX_RANKS sources], in every rank's workspace
+  long off_counts;   // uint32 [2] arrival counters of this rank's CTAs (zero between launches)
+  long off_push;     // bf16 [world sources][t_max][H] pushed partial rows (this call's parity)
+  long off_resid;    // bf16 [t_max][H] residual; a rank keeps its owned rows current
+  long off_normed;   // bf16 [t_max][H] normed rows, complete on every rank after the launch
+  uint32_t* epoch;   // local epoch word, bumped once per launch
+  const __nv_bfloat16* gamma;
+  float eps;
+  unsigned long long timeout_ns;
+};
+
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
@@ -83,6 +105,7 @@ struct GemmParams {
   int push_mode, my_rank, world, push_rows;
   long slot_stride;                  // elements between source slots in a destination buffer
   unsigned long long peer_base[8];   // destination buffer base (as mapped here) per rank
+  ArTail ar;
 };
 
 // owner rank of token row t when `rows` tokens are split into `world` near-equal ranges
@@ -440,6 +463,19 @@ __device__ __forceinline__ void stage_flush_bf16(const GemmParams& p, uint32_t s
     const int n = n0 + j, f = f0 + c8;
     if (n >= p.N || f >= f_lim) continue;
     const uint4 v = lds_u4(stage + (uint32_t)(j * fw + c8) * 2);
+    if (p.push_mode != 0) {
+      // fused reduce-scatter: the token row goes to slot `my_rank` of its owner rank (mode 1) or
+      // of every rank (mode 2), over NVLink; rows there are 16-byte aligned (H % 8 == 0)
+      const long off = (long)p.my_rank * p.slot_stride + (long)n * p.ldo + f;
+      if (p.push_mode == 1) {
+        const int d = row_owner(n, p.push_rows, p.world);
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.peer_base[d]) + off) = v;
+      } else {
+        for (int d = 0; d < p.world; ++d)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.peer_base[d]) + off) = v;
+      }
+      continue;
+    }
     __nv_bfloat16* dst = out + (long)n * p.ldo + f;
     if (p.vec_out && f + 8 <= f_lim) {
       *reinterpret_cast<uint4*>(dst) = v;
@@ -938,6 +974,188 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
   if (trace && et == 0) trace[9] = globaltimer_ns();
 }
 
+// ----------------------------------------------------------------------------------------------
+// Fused all-reduce tail (swap-AB bf16 GEMM with push mode 1; epilogue warps, 128 threads).
+//
+// Protocol of one launch, epoch e = local epoch word + 1:
+//  phase 0  every CTA has pushed its partial rows (each storing thread fenced at system scope);
+//           the last of this rank's CTAs to arrive (gpu-scope arrival counter) raises flag[0][rank]
+//           = e in every rank's workspace;
+//  reduce   CTA i < min(owned rows, grid) waits (bounded) for flag[0][*] >= e from every rank,
+//           sums its owned rows over the ranks' pushed slots (fp32, source order), adds the
+//           residual (stored back rounded to bf16, locally), applies RMSNorm to the rounded value
+//           and stores the normed row into every rank;
+//  phase 1  the last reducing CTA raises flag[1][rank] = e everywhere (a rank that owns no rows
+//           raises it from CTA 0 at once);
+//  exit     CTA 0 waits (bounded) for flag[1][*] >= e from every rank, then stores e as the new
+//           epoch. The next kernel's griddepcontrol.wait therefore sees every normed row.
+// Flags only grow, so nothing is reset between launches; the arrival counters are reset by the
+// CTA that completes them. A slot is rewritten only by the next launch, which cannot start its
+// pushes before every rank left this one (phase 1), so one set of push slots would do; the caller
+// still alternates two. Every wait records ERR_PEER_TIMEOUT and gives up after `timeout_ns`.
+// ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t* ar_flag(const ArTail& a, int dst, int phase, int src) {
+  return reinterpret_cast<uint32_t*>(a.ws[dst] + a.off_flags) + phase * AR_TAIL_MAX_RANKS + src;
+}
+
+// Arrival of this CTA at `phase`; the CTA completing `expected` arrivals signals every rank.
+__device__ __forceinline__ void ar_arrive(const ArTail& a, int phase, uint32_t e, uint32_t expected, int et) {
+  named_bar_sync(1, 128);  // every thread of the CTA fenced its stores before this barrier
+  if (et == 0) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(a.ws[a.rank] + a.off_counts) + phase;
+    fence_acq_rel_sys();
+    const uint32_t old = atom_add_acq_rel_gpu(cnt, 1u);
+    if (old + 1u == expected) {
+      st_relaxed_gpu(cnt, 0u);
+      fence_acq_rel_sys();
+      for (int d = 0; d < a.world; ++d) st_release_sys(ar_flag(a, d, phase, a.rank), e);
+    }
+  }
+}
+
+// Bounded wait for flag[phase][src] >= e from every rank; uniform result across the 128 threads.
+__device__ __forceinline__ bool ar_wait(const GemmParams& p, int phase, uint32_t e, int et, volatile int* s_ok) {
+  const ArTail& a = p.ar;
+  if (et == 0) *s_ok = 1;
+  named_bar_sync(1, 128);
+  if (et < a.world && !wait_flag_geq(ar_flag(a, a.rank, phase, et), e, a.timeout_ns, p.err)) *s_ok = 0;
+  named_bar_sync(1, 128);
+  return *s_ok != 0;
+}
+
+// One owned token row: H features, 8 per 16-byte chunk, chunks et + 128 j (j < MAXC), summed in
+// groups of 4 chunks (fp32 accumulators of one group live at a time; the rounded residual of every
+// chunk is kept packed for the normalisation pass).
+template <int MAXC>
+__device__ __forceinline__ void ar_tail_row(const ArTail& a, long row, int et, volatile float* red) {
+  const int nvec = a.H / 8;
+  uint4* resid = reinterpret_cast<uint4*>(a.ws[a.rank] + a.off_resid) + row * nvec;
+  uint4 packed[MAXC];
+  float ss = 0.f;
+#pragma unroll
+  for (int g0 = 0; g0 < MAXC; g0 += 4) {
+    float acc[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = et + 128 * (g0 + j);
+      if (c < nvec) {
+        const uint4 r = resid[c];
+        const uint32_t* ru = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) unpack_bf16x2(ru[q], acc[j][2 * q], acc[j][2 * q + 1]);
+      }
+    }
+    // sources in rank order (deterministic); a source's chunks are all loaded before any is added
+#pragma unroll
+    for (int src = 0; src < AR_TAIL_MAX_RANKS; ++src) {
+      if (src >= a.world) break;
+      const uint4* part = reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.ws[a.rank] + a.off_push) + ((long)src * a.t_max + row) * a.H);
+      uint4 d[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = et + 128 * (g0 + j);
+        if (c < nvec) d[j] = __ldcg(part + c);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = et + 128 * (g0 + j);
+        if (c < nvec) {
+          const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float x0, x1;
+            unpack_bf16x2(du[q], x0, x1);
+            acc[j][2 * q] += x0;
+            acc[j][2 * q + 1] += x1;
+          }
+        }
+      }
+    }
+    // the residual is stored rounded to bf16 and the norm is taken of that stored value
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = et + 128 * (g0 + j);
+      if (c < nvec) {
+        uint32_t* pu = reinterpret_cast<uint32_t*>(&packed[g0 + j]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          pu[q] = pack_bf16x2(acc[j][2 * q], acc[j][2 * q + 1]);
+          float r0, r1;
+          unpack_bf16x2(pu[q], r0, r1);
+          ss += r0 * r0 + r1 * r1;
+        }
+        resid[c] = packed[g0 + j];
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((et & 31) == 0) red[et >> 5] = ss;
+  named_bar_sync(1, 128);
+  const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / (float)a.H + a.eps);
+  named_bar_sync(1, 128);  // `red` is reused by the next row
+  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j) {
+    const int c = et + 128 * j;
+    if (c < nvec) {
+      const uint4 g = gv[c];
+      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&g);
+      const uint32_t* pu = reinterpret_cast<const uint32_t*>(&packed[j]);
+      uint4 o;
+      uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float r0, r1, g0, g1;
+        unpack_bf16x2(pu[q], r0, r1);
+        unpack_bf16x2(gu[q], g0, g1);
+        ou[q] = pack_bf16x2(r0 * inv * g0, r1 * inv * g1);
+      }
+      const long off = a.off_normed + (row * nvec + c) * 16;
+      if (a.mc) {
+        multimem_st_16(reinterpret_cast<void*>(a.mc + off), o);
+      } else {
+        for (int d = 0; d < a.world; ++d) *reinterpret_cast<uint4*>(a.ws[d] + off) = o;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void ar_tail(const GemmParams& p, const Smem& s, int et) {
+  const ArTail& a = p.ar;
+  volatile uint32_t* s_e = reinterpret_cast<volatile uint32_t*>(s.epi);  // [0] epoch, [1] ok
+  volatile float* red = reinterpret_cast<volatile float*>(s.epi) + 4;  // [4] sum-of-squares partials
+  if (et == 0) s_e[0] = *a.epoch + 1u;
+  named_bar_sync(1, 128);
+  const uint32_t e = s_e[0];
+  ar_arrive(a, 0, e, gridDim.x, et);
+  const int base = a.T / a.world, extra = a.T % a.world;
+  const long r0 = (long)a.rank * base + min(a.rank, extra);
+  const int nrows = base + (a.rank < extra ? 1 : 0);
+  const int nred = min(nrows, (int)gridDim.x);
+  volatile int* s_ok = reinterpret_cast<volatile int*>(s_e + 1);
+  if ((int)blockIdx.x < nred) {
+    if (ar_wait(p, 0, e, et, s_ok)) {
+      for (long row = r0 + blockIdx.x; row < r0 + nrows; row += gridDim.x) {
+        if (a.H <= 128 * 8 * 4)
+          ar_tail_row<4>(a, row, et, red);
+        else
+          ar_tail_row<8>(a, row, et, red);
+      }
+    }
+    __threadfence_system();  // this thread's normed stores (peer or multicast) before the signal
+    ar_arrive(a, 1, e, nred, et);
+  } else if (nred == 0 && blockIdx.x == 0 && et == 0) {
+    fence_acq_rel_sys();
+    for (int d = 0; d < a.world; ++d) st_release_sys(ar_flag(a, d, 1, a.rank), e);
+  }
+  if (blockIdx.x == 0) {
+    ar_wait(p, 1, e, et, s_ok);
+    if (et == 0) *a.epoch = e;
+  }
+}
+
 template <int EPI, bool TRANS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -1160,9 +1378,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (k < n16) tmem_ld16(taddr_row + col + 16 * k, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * k]));
         tmem_ld_wait_tied(r);
       };
-      if (sg.ncontrib == 1 && p.push_mode == 0 && p.direct_epi) {
+      // the staged swap-AB bf16 store is push-aware; other whole-tile epilogues write `out` only
+      constexpr bool kPushDirect = TRANS && EPI == EPI_STORE_BF16;
+      const bool direct = p.direct_epi && (p.push_mode == 0 || kPushDirect);
+      if (sg.ncontrib == 1 && direct) {
         direct_epilogue<EPI, TRANS>(p, s, fetch_tmem, row, lane, quarter, sg.tm, sg.tn, &s.tempty[acc]);
-      } else if (sg.ncontrib > 1 && sg.contrib == 0 && p.push_mode == 0 && p.direct_epi) {
+      } else if (sg.ncontrib > 1 && sg.contrib == 0 && direct) {
         // stream-K owner: wait (bounded) for the other contributors' partials, then run the
         // whole-tile epilogue on own accumulator + partials, read per row straight from the
         // workspace in contributor order (deterministic)
@@ -1343,6 +1564,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+  if constexpr (TRANS && EPI == EPI_STORE_BF16) {
+    // fused all-reduce tail: TMEM is already released, so cross-GPU waits hold no tensor memory
+    if (p.ar.on && warp >= 2) ar_tail(p, s, threadIdx.x - 64);
   }
   if (trace && threadIdx.x == 0) trace[7] = globaltimer_ns();
 }
@@ -1534,7 +1759,8 @@ static Plan make_plan(int M, int N, int K, int bn, int num_sms, int force_mode, 
     pl.dp_tiles = pl.tiles;
     return pl;
   }
-  if (trans && !push && (force_mode == 3 || (force_mode == 0 && ck_enabled() && pl.tiles < num_sms))) {
+  if (trans && (!push || epi == EPI_STORE_BF16) &&
+      (force_mode == 3 || (force_mode == 0 && ck_enabled() && pl.tiles < num_sms))) {
     const int C = pick_ck(pl.tiles, kb, num_sms, epi, bn, kbox);
     if (C >= 2) {
       pl.ck = C;
@@ -1586,7 +1812,8 @@ struct RopeArgs {
 
 static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, bool trans,
                       int64_t bn_req, int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
-                      const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push, const RopeArgs* rope) {
+                      const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push, const RopeArgs* rope,
+                      const ArTail* ar = nullptr) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm_tcgen05: tensors must be CUDA");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_tcgen05: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tcgen05: A [M,K], B [N,K]");
@@ -1619,7 +1846,8 @@ static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
   Plan pl = make_plan(M, N, K, bn, sms, (int)mode, (int)epi, trans, !push.empty(), kbox);
   p.ck = pl.ck;
   TORCH_CHECK(mode != 3 || pl.ck >= 2, "gemm_tcgen05: cluster split-K requested but not possible for this shape");
-  TORCH_CHECK(p.ck <= 1 || (trans && push.empty()), "gemm_tcgen05: cluster split-K needs swap-AB and no push");
+  TORCH_CHECK(p.ck <= 1 || (trans && (push.empty() || epi == EPI_STORE_BF16)),
+              "gemm_tcgen05: cluster split-K needs swap-AB (and the bf16 epilogue when pushing)");
   const SmemPlan sp = smem_plan(bn, p.ck, kbox, (int)epi, trans);
   TORCH_CHECK(sp.bytes <= SMEM_BUDGET, "gemm_tcgen05: shared memory plan exceeds the budget");
   const int stages = sp.stages;
@@ -1665,6 +1893,13 @@ static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
     p.ldo = push[5];
     TORCH_CHECK(p.world >= 1 && p.world <= 8 && (int)push.size() == 6 + p.world, "push: peer table");
     for (int i = 0; i < p.world; ++i) p.peer_base[i] = (unsigned long long)push[6 + i];
+  }
+  if (ar != nullptr) {
+    TORCH_CHECK(trans && epi == EPI_STORE_BF16 && p.push_mode == 1 && ar->world == p.world && ar->rank == p.my_rank &&
+                    ar->T == N && ar->H == M,
+                "fused all-reduce tail: swap-AB bf16 GEMM pushing rows to their owners");
+    p.ar = *ar;
+    p.ar.on = 1;
   }
   if (trace.has_value()) {
     TORCH_CHECK(trace->numel() >= (int64_t)pl.grid * 16 && trace->scalar_type() == at::kLong, "gemm trace buffer");
@@ -1734,6 +1969,47 @@ void gemm_qkv_rope(const at::Tensor& w, const at::Tensor& x, at::Tensor& q_out, 
   r.hkv = (int)hkv;
   r.ps = (int)kcache.size(2);
   gemm_impl(w, x, q_out, EPI_QKV_ROPE, true, 0, mode, workspace, counters, err, c10::nullopt, {}, &r);
+}
+
+// Decode o_proj / down_proj with the tensor-parallel all-reduce, residual add and RMSNorm fused
+// in (see ar_tail): w [H, K] weights, x [T, K] activations; the partial rows go to their owner
+// ranks' push slots, and after the launch every rank's `normed` holds RMSNorm(resid + sum) * gamma
+// for all T rows while each rank's `resid` holds the updated rows it owns.
+// push = [1, my_rank, world, T, slot_stride, H, push slot base of each rank (as mapped here)...]
+// cfg  = [t_max, off_flags, off_counts, off_push, off_resid, off_normed, multicast base, timeout ns,
+//         workspace base of each rank...]; `part` is this rank's local push slot (shape checks only).
+void gemm_allreduce_norm(const at::Tensor& w, const at::Tensor& x, at::Tensor& part, const std::vector<int64_t>& push,
+                         const std::vector<int64_t>& cfg, const at::Tensor& gamma, double eps, at::Tensor& epoch,
+                         int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err) {
+  const int64_t T = x.size(0), H = w.size(0);
+  TORCH_CHECK(push.size() >= 6 && push[0] == 1 && push[3] == T && push[5] == H, "gemm_allreduce_norm: push table");
+  const int world = (int)push[2];
+  TORCH_CHECK(world >= 1 && world <= AR_TAIL_MAX_RANKS && (int64_t)cfg.size() == 8 + world,
+              "gemm_allreduce_norm: config table");
+  TORCH_CHECK(H % 8 == 0 && H <= 128 * 8 * 8, "gemm_allreduce_norm: H % 8 == 0 and H <= 8192");
+  TORCH_CHECK(T <= cfg[0], "gemm_allreduce_norm: T exceeds the workspace rows");
+  TORCH_CHECK(gamma.is_cuda() && gamma.scalar_type() == at::kBFloat16 && gamma.numel() == H && gamma.is_contiguous(),
+              "gemm_allreduce_norm: gamma bf16 [H]");
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() >= 1, "gemm_allreduce_norm: epoch");
+  TORCH_CHECK(cfg[6] % 16 == 0, "gemm_allreduce_norm: multicast base must be 16-byte aligned");
+  ArTail a{};
+  a.rank = (int)push[1];
+  a.world = world;
+  a.T = (int)T;
+  a.H = (int)H;
+  a.t_max = (int)cfg[0];
+  a.off_flags = cfg[1];
+  a.off_counts = cfg[2];
+  a.off_push = cfg[3];
+  a.off_resid = cfg[4];
+  a.off_normed = cfg[5];
+  a.mc = (unsigned long long)cfg[6];
+  a.timeout_ns = (unsigned long long)cfg[7];
+  for (int i = 0; i < world; ++i) a.ws[i] = (unsigned long long)cfg[8 + i];
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr());
+  a.eps = (float)eps;
+  gemm_impl(w, x, part, EPI_STORE_BF16, true, 0, mode, workspace, counters, err, c10::nullopt, push, nullptr, &a);
 }
 
 // [bn, workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters, cluster split]

@@ -7,7 +7,8 @@ Per layer (reference ``forward_layer``, ``agent/src/inference/forward_pass.rs:19
                                                           prefill: rope_kv_write)
     attn  = paged GQA attention                           (decode: split-KV; prefill: flash)
     part  = tcgen05 GEMM(attn, wo)                        -> own slot of the symmetric workspace
-    resid, normed = AR(part) + resid, RMSNorm(mlp_norm)   (ar_fused_norm over NVLink; TP=1: add_rmsnorm)
+    resid, normed = AR(part) + resid, RMSNorm(mlp_norm)   (ar_fused_norm over NVLink; TP=1: add_rmsnorm;
+                                                          decode TP>1: one launch, gemm_allreduce_norm)
     h     = tcgen05 GEMM(normed, wgu) with SiLU(gate)*up epilogue
     part  = tcgen05 GEMM(h, wdown)
     resid, normed = AR(part) + resid, RMSNorm(next attn_norm or final_norm)
@@ -102,6 +103,11 @@ class LlamaRunner:
         # "push": the o_proj / down GEMM epilogues scatter partial rows to their owner ranks over
         # NVLink (fused GEMM -> reduce-scatter); otherwise GEMMs write locally and the AR kernel pulls
         self.push_rs = self.use_fused_ar and ecfg.allreduce_impl in ("push", "push_oneshot")
+        # decode-sized steps run o_proj / down_proj with the all-reduce, residual add and RMSNorm in
+        # the GEMM's own launch ("auto"); MESH_GEMM_AR=0 or an explicit all-reduce choice keeps the
+        # separate all-reduce kernel
+        self.gemm_ar = (self.use_fused_ar and ecfg.allreduce_impl == "auto" and self.H % 8 == 0 and
+                        self.H <= 8192 and os.environ.get("MESH_GEMM_AR", "1") != "0")
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
@@ -159,6 +165,18 @@ class LlamaRunner:
             scratch[key] = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
         return scratch[key]
 
+    def _proj_reduce(self, x: torch.Tensor, wt: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor,
+                     gamma: torch.Tensor, parity: int, bufs: dict):
+        """resid += sum_ranks(x @ wt.T); normed = RMSNorm(resid) * gamma (row-parallel projection)."""
+        T = x.shape[0]
+        if self.gemm_ar and T <= ops.SWAP_AB_MAX_TOKENS:
+            self.symm.gemm_allreduce_norm(x, wt, parity, gamma, self.cfg.rms_norm_eps,
+                                          multicast=self.world >= 8)
+            return
+        part = self._part_buf(T, parity, bufs)
+        ops.linear(x, wt, out=part, push=self._push(T, parity))
+        self._reduce(part, resid, normed, gamma, parity)
+
     # ------------------------------------------------------------------------------------------
     def forward(self, m: StepMeta, bufs: Optional[dict] = None) -> torch.Tensor:
         """Run all layers and the LM head; returns next-token ids [S] (int32, greedy)."""
@@ -201,15 +219,11 @@ class LlamaRunner:
             else:
                 ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
                                  self.window)
-            part = self._part_buf(T, parity, bufs)
-            ops.linear(attn, L.wo, out=part, push=self._push(T, parity))
-            self._reduce(part, resid, normed, L.mlp_norm, parity)
+            self._proj_reduce(attn, L.wo, resid, normed, L.mlp_norm, parity, bufs)
             parity ^= 1
             ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
-            part = self._part_buf(T, parity, bufs)
-            ops.linear(h, L.wdown, out=part, push=self._push(T, parity))
             gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
-            self._reduce(part, resid, normed, gamma, parity)
+            self._proj_reduce(h, L.wdown, resid, normed, gamma, parity, bufs)
             parity ^= 1
             rng(None)
 

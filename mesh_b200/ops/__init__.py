@@ -131,6 +131,23 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, epi: int = EPI_STO
 _PLANS = {}
 
 
+def gemm_allreduce_norm(w: torch.Tensor, x: torch.Tensor, part_view: torch.Tensor, push: list, cfg: list,
+                        gamma: torch.Tensor, eps: float, epoch: torch.Tensor, mode: int = 0):
+    """Swap-AB decode GEMM x @ w.T whose epilogue pushes partial rows to their owner ranks, with the
+    tensor-parallel reduction, residual add, RMSNorm and all-gather of the normed rows in the same
+    launch (``parallel.symm.SymmWorkspace.gemm_allreduce_norm`` builds the tables)."""
+    s = scratch(x.device)
+    M, N, K = w.shape[0], x.shape[0], w.shape[1]
+    key = (M, N, K, EPI_STORE_BF16, True, x.device.index)
+    plan = _PLANS.get(key)
+    if plan is None:
+        plan = _PLANS[key] = ext().gemm_plan(M, N, K, EPI_STORE_BF16, True, x.device.index)
+    if plan[2] > 0:
+        s.ensure_gemm(plan[1], plan[2])
+    ext().gemm_allreduce_norm(w, x, part_view, push, cfg, gamma, eps, epoch, mode, s.gemm_ws, s.gemm_counters, s.err)
+    _count()
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, epi: int = EPI_STORE_BF16,
            swap_ab: Optional[bool] = None, push: Optional[list] = None) -> torch.Tensor:
     """y = x @ w.T for x [T, K], w [N, K] (nn.Linear layout). Decode-sized T uses swap-AB so the

@@ -3,13 +3,17 @@
 One allocation per rank, mapped into every peer of the TP group (CUDA VMM/IPC through
 ``torch.distributed._symmetric_memory``). Layout (byte offsets, identical on every rank):
 
-    [flags: 2 phases x 256 blocks x 8 ranks x u32] [partial slot 0: T_max x H bf16]
-    [partial slot 1] [resid: T_max x H bf16] [normed: T_max x H bf16]
+    [flags: 2 phases x 256 blocks x 8 ranks x u32] [fused-GEMM flags: 2 phases x 8 ranks x u32]
+    [fused-GEMM arrival counters: 2 x u32] [partial slot 0: T_max x H bf16] [partial slot 1]
+    [resid: T_max x H bf16] [normed: T_max x H bf16] [push slots, parity 0 and 1: world x T_max x H]
 
 The o_proj / down_proj GEMMs write their partial sums into a partial slot; the ``ar_fused_norm``
 kernel reads the peers' slots over NVLink, adds the residual, applies RMSNorm and writes
-``resid`` / ``normed`` (locally for one-shot, into every peer for two-shot). Peer memory is touched
-by plain P2P loads and stores, or, when the allocation is bound to an NVLink multicast object
+``resid`` / ``normed`` (locally for one-shot, into every peer for two-shot). For decode-sized steps
+``gemm_allreduce_norm`` does all of it in the GEMM's own launch: the epilogue pushes each partial
+token row into the push slot of the rank that owns the row, and the same kernel then reduces the
+owned rows, adds the residual, applies RMSNorm and writes the normed rows into every rank. Peer
+memory is touched by plain P2P loads and stores, or, when the allocation is bound to an NVLink multicast object
 (NVSwitch NVLS), by ``multimem`` loads that return the sum over all ranks and ``multimem`` stores
 that write every rank at once. No TMA (and no multicast TMA) ever reads a peer address.
 """
@@ -35,6 +39,8 @@ class SymmLayout:
     hidden: int
     world: int
     off_flags: int
+    off_gflags: int
+    off_gcount: int
     off_p0: int
     off_p1: int
     off_resid: int
@@ -48,6 +54,8 @@ class SymmLayout:
         row = t_max * hidden * 2
         o = 0
         off_flags = o; o = _align(o + flags_bytes)
+        off_gflags = o; o = _align(o + 2 * 8 * 4)
+        off_gcount = o; o = _align(o + 2 * 4)
         off_p0 = o; o = _align(o + row)
         off_p1 = o; o = _align(o + row)
         off_resid = o; o = _align(o + row)
@@ -55,7 +63,8 @@ class SymmLayout:
         # fused reduce-scatter targets: per parity, one [t_max, H] slot per source rank
         off_push0 = o; o = _align(o + world * row)
         off_push1 = o; o = _align(o + world * row)
-        return cls(t_max, hidden, world, off_flags, off_p0, off_p1, off_resid, off_normed, off_push0, off_push1, o)
+        return cls(t_max, hidden, world, off_flags, off_gflags, off_gcount, off_p0, off_p1, off_resid, off_normed,
+                   off_push0, off_push1, o)
 
 
 class SymmWorkspace:
@@ -82,6 +91,7 @@ class SymmWorkspace:
         if delta != 0:
             raise RuntimeError(f"symmetric workspace is at offset {delta} inside its allocation")
         self.bases = torch.tensor(ptrs, dtype=torch.int64)
+        self._bases = [int(b) for b in ptrs]
         # NVLS multicast address of the same allocation (0: plain peer loads). MESH_NVLS=0 turns it off.
         if multicast is None:
             multicast = os.environ.get("MESH_NVLS", "1") != "0"
@@ -96,6 +106,7 @@ class SymmWorkspace:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
         self.mc_base = mc if int(flag.item()) == 1 else 0
         self.epoch = torch.zeros(256, dtype=torch.int32, device=device)
+        self.gepoch = torch.zeros(1, dtype=torch.int32, device=device)  # fused GEMM + all-reduce launches
         self._no_trace = torch.empty(0, dtype=torch.int64, device=device)
         dist.barrier(self.group)
 
@@ -154,6 +165,23 @@ class SymmWorkspace:
                                       two_shot, timeout_s)
         ops._count()
 
+    def gemm_allreduce_norm(self, x: torch.Tensor, w: torch.Tensor, parity: int, gamma: torch.Tensor, eps: float,
+                            timeout_s: float = 5.0, mode: int = 0, multicast: bool = True):
+        """One launch: partial = x @ w.T on this rank, summed over the TP group, added to ``resid``
+        and RMS-normalised into ``normed`` on every rank. Decode-sized T (swap-AB GEMM). Each rank
+        keeps only the ``resid`` rows it owns current (the same rows in every call with this T);
+        ``multicast`` writes the normed rows with NVLS stores when the workspace has them."""
+        L = self.layout
+        T = x.shape[0]
+        if T > L.t_max:
+            raise ValueError(f"T={T} exceeds symmetric workspace capacity {L.t_max}")
+        off = L.off_push0 if parity % 2 == 0 else L.off_push1
+        push = [1, self.rank, self.world, T, L.t_max * L.hidden, L.hidden] + [int(b) + off for b in self._bases]
+        cfg = [L.t_max, L.off_gflags, L.off_gcount, off, L.off_resid, L.off_normed,
+               self.mc_base if multicast else 0, int(timeout_s * 1e9)] + self._bases
+        local = self.view(off + self.rank * L.t_max * L.hidden * 2, T)
+        ops.gemm_allreduce_norm(w, x, local, push, cfg, gamma, eps, self.gepoch, mode)
+
     def reset(self):
         """Collective: zero the flags and epoch counters on every rank. Needed after a timed-out
         collective left the ranks' epochs out of step."""
@@ -161,6 +189,7 @@ class SymmWorkspace:
         dist.barrier(self.group)
         self.buf[: self.layout.off_p0].zero_()
         self.epoch.zero_()
+        self.gepoch.zero_()
         ops.scratch(self.device).err.zero_()
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)

@@ -76,3 +76,153 @@ def test_single_slot_protocol_is_caught():
         if found:
             break
     assert found is not None
+
+
+# ------------------------------------------------------------------------------------------------
+# The decode GEMM with the all-reduce in its own launch (gemm_tcgen05.cu, ar_tail).
+#
+# Per rank, launch i runs `ctas` CTAs at once; each CTA pushes its part of every token row into
+# the owner rank's push slot (i % slots) and arrives on phase 0 (the last local arrival raises the
+# rank's phase-0 flag = i + 1 everywhere). The owner's reducing CTA waits for every rank's phase-0
+# flag, reads all sources' parts of its row, writes the normed row into every rank and arrives on
+# phase 1; a rank that owns no row raises its phase-1 flag from CTA 0 right away. CTA 0 waits for
+# every rank's phase-1 flag; the launch ends when all CTAs finished, and then the next kernel (the
+# consumer) reads the normed rows before launch i + 1 starts.
+# ------------------------------------------------------------------------------------------------
+def run_gemm_ar_protocol(world, ctas, rows, calls, schedule, slots=2, wait0=True, wait1=True):
+    owner_of = [r for r in range(rows)]                   # rank r owns row r (rows <= world)
+    slot = [[[[-1] * ctas for _ in range(world)] for _ in range(slots)] for _ in range(world)]
+    normed = [[-1] * rows for _ in range(world)]           # normed[rank][row] = call that wrote it
+    flags = [[[0] * world for _ in range(2)] for _ in range(world)]  # flags[rank][phase][src]
+    count = [[0, 0] for _ in range(world)]
+    reading_slot = [set() for _ in range(world)]           # slots a rank's reducer is reading
+    reading_normed = [False] * world
+    call = [0] * world
+    progs, pcs = {}, {}
+
+    def program(r, c):
+        p = [("push",), ("arrive", 0)]
+        owns = r < rows
+        if c == 0 and owns:
+            p += ([("wait", 0)] if wait0 else []) + [("read_start",), ("read_end",), ("write_normed",), ("arrive", 1)]
+        if c == 0 and not owns:
+            p += [("signal", 1)]
+        if c == 0:
+            p += [("wait", 1)] if wait1 else []
+        return p
+
+    def start_launch(r):
+        for c in range(ctas):
+            progs[(r, c)] = program(r, c)
+            pcs[(r, c)] = 0
+        progs[(r, "consumer")] = None
+
+    for r in range(world):
+        start_launch(r)
+    k = 0
+    while True:
+        live = [key for key, p in progs.items() if p is not None and pcs.get(key, 0) < len(p)]
+        # a rank whose CTAs are all done runs its consumer, then the next launch
+        for r in range(world):
+            if call[r] >= calls:
+                continue
+            if all(pcs[(r, c)] >= len(progs[(r, c)]) for c in range(ctas)) and progs[(r, "consumer")] is None:
+                progs[(r, "consumer")] = [("cread_start",), ("cread_end",)]
+                pcs[(r, "consumer")] = 0
+                live.append((r, "consumer"))
+        if not live:
+            break
+        movable = []
+        for key in live:
+            op = progs[key][pcs[key]]
+            r = key[0]
+            e = call[r] + 1
+            if op[0] == "wait" and min(flags[r][op[1]]) < e:
+                continue
+            movable.append(key)
+        if not movable:
+            return "deadlock"
+        key = movable[schedule[k % len(schedule)] % len(movable)] if schedule else movable[0]
+        k += 1
+        r, c = key
+        i = call[r]
+        e = i + 1
+        s = i % slots
+        op = progs[key][pcs[key]]
+        if op[0] == "push":
+            for d in range(world):
+                if s in reading_slot[d]:
+                    return f"rank {r} cta {c} pushes call {i} into slot {s} of rank {d} during its read"
+                slot[d][s][r][c] = i
+        elif op[0] == "arrive":
+            ph = op[1]
+            count[r][ph] += 1
+            expect = ctas if ph == 0 else 1
+            if count[r][ph] == expect:
+                count[r][ph] = 0
+                for d in range(world):
+                    flags[d][ph][r] = e
+        elif op[0] == "signal":
+            for d in range(world):
+                flags[d][op[1]][r] = e
+        elif op[0] == "read_start":
+            for src in range(world):
+                for cc in range(ctas):
+                    if slot[r][s][src][cc] != i:
+                        return f"rank {r} reduces call {i} but slot {s} holds call {slot[r][s][src][cc]} of {src}"
+            reading_slot[r].add(s)
+        elif op[0] == "read_end":
+            reading_slot[r].discard(s)
+        elif op[0] == "write_normed":
+            for d in range(world):
+                if reading_normed[d]:
+                    return f"rank {r} writes normed row (call {i}) into rank {d} while its consumer reads"
+                normed[d][owner_of.index(r)] = i
+        elif op[0] == "cread_start":
+            for row in range(rows):
+                if normed[r][row] != i:
+                    return f"consumer of rank {r} reads row {row} from call {normed[r][row]}, wanted {i}"
+            reading_normed[r] = True
+        elif op[0] == "cread_end":
+            reading_normed[r] = False
+            call[r] += 1
+            progs[(r, "consumer")] = None
+            if call[r] < calls:
+                start_launch(r)
+            else:
+                for cc in range(ctas):
+                    progs[(r, cc)] = None
+            continue
+        pcs[key] += 1
+    return None
+
+
+@settings(max_examples=300, deadline=None)
+@given(world=st.integers(1, 8), ctas=st.integers(1, 3), rows_frac=st.integers(0, 8), calls=st.integers(1, 4),
+       slots=st.integers(1, 2), schedule=st.lists(st.integers(0, 63), min_size=1, max_size=300))
+def test_gemm_allreduce_two_phase_protocol_has_no_race(world, ctas, rows_frac, calls, slots, schedule):
+    """No race with two push slots, nor with one: phase 1 already keeps the next launch's pushes
+    away from a slot that is still being read."""
+    rows = max(1, min(world, rows_frac))
+    assert run_gemm_ar_protocol(world, ctas, rows, calls, schedule, slots=slots) is None
+
+
+def _find_violation(**kw):
+    import random
+    for seed in range(3000):
+        rng = random.Random(seed)
+        sched = [rng.randrange(64) for _ in range(120)]
+        v = run_gemm_ar_protocol(3, 2, 2, 3, sched, **kw)
+        if v:
+            return v
+    return None
+
+
+def test_gemm_allreduce_protocol_without_phase0_wait_is_caught():
+    """A reducer that does not wait for every rank's pushes reads an incomplete row."""
+    assert _find_violation(wait0=False) is not None
+
+
+def test_gemm_allreduce_protocol_without_phase1_wait_is_caught():
+    """Without CTA 0's final wait the consumer can read normed rows a peer has not written yet."""
+    assert _find_violation(wait1=False) is not None

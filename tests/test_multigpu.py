@@ -1,11 +1,15 @@
-"""Tensor-parallel paths on 2 GPUs, run as spawned child processes (NCCL for plumbing with its NVLS
-off; the fused kernels on plain peer loads, except the test that checks their NVLS multicast path).
+"""Tensor-parallel paths on 2, 4 and 8 GPUs (and the fused GEMM + all-reduce launch on one), run as
+spawned child processes (NCCL for plumbing with its NVLS off; the fused kernels on plain peer loads,
+except the tests that check their NVLS multicast path).
 
 * the fused peer-memory all-reduce + residual + RMSNorm kernel (one-shot and two-shot) against an
   fp32 reference built from NCCL all-gathered partials;
+* the decode GEMM with the all-reduce, residual add, RMSNorm and all-gather in the same launch, for
+  every GEMM schedule, against the same reference;
 * the bounded-wait error path: a rank that never joins makes the other's wait run out, the kernel
   returns ERR_PEER_TIMEOUT within the limit, and a collective reset makes the workspace usable;
-* the TP=2 decoder's logits against TP=1.
+* the TP=N decoder's prefill and decode logits against TP=1.
+A test needing more GPUs than the machine has is skipped.
 """
 import os
 import socket
@@ -16,8 +20,6 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-
-NEED = 2
 
 
 def _free_port():
@@ -139,6 +141,55 @@ def _push_check(rank, world):
         parity ^= 1
 
 
+def _gemm_ar_check(rank, world, multicast=False):
+    """Decode o_proj/down GEMM with the all-reduce, residual add and RMSNorm in its own launch: the
+    owned residual rows and every normed row against fp32 sums of NCCL all-gathered partials, for
+    the automatic schedule and each forced one (whole tiles, stream-K, cluster split-K), several
+    launches in a row over alternating push slots."""
+    import torch.distributed as dist
+    from mesh_b200 import ops
+    from mesh_b200.models.sharding import even_split
+    from mesh_b200.ops import reference as ref
+    from mesh_b200.parallel.symm import SymmWorkspace
+    dev = torch.device("cuda", rank)
+    H = 4096
+    ws = SymmWorkspace(256, H, dev, multicast=multicast)
+    if multicast and not ws.mc_base:
+        return "symmetric memory has no NVLS multicast mapping on this node"
+    gamma = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(3))).to(torch.bfloat16).to(dev)
+    parity = 0
+    cases = [(512, 64, 0), (2048, 64, 0), (1792, 64, 0), (512, 1, 0), (2048, 5, 0), (1024, 256, 0),
+             (1024, 64, 1), (2048, 64, 2), (2048, 64, 3), (2048, 16, 3)]
+    for i, (K, T, mode) in enumerate(cases):
+        g = torch.Generator().manual_seed(1000 * i + rank)
+        w = (torch.randn(H, K, generator=g) * 0.03).to(torch.bfloat16).to(dev)
+        x = torch.randn(T, K, generator=g).to(torch.bfloat16).to(dev)
+        resid0 = torch.randn(T, H, generator=torch.Generator().manual_seed(77 + i)).to(torch.bfloat16).to(dev)
+        for rep in range(2):  # back-to-back launches: epochs, counters and both push slots are reused
+            ws.resid(T).copy_(resid0)
+            ws.normed(T).fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            ws.gemm_allreduce_norm(x, w, parity, gamma, 1e-5, timeout_s=5.0, mode=mode, multicast=multicast)
+            torch.cuda.synchronize()
+            ops.scratch(dev).check(f"gemm_ar K={K} T={T} mode={mode}")
+            part = (x.float() @ w.float().T).to(torch.bfloat16)
+            allp = torch.empty(world, T, H, dtype=torch.bfloat16, device=dev)
+            dist.all_gather_into_tensor(allp.view(-1), part.contiguous().view(-1))
+            want_r = (resid0.float() + allp.float().sum(0)).to(torch.bfloat16)
+            want_n = ref.rmsnorm(want_r.float(), gamma, 1e-5)
+            r0, nr = even_split(T, world, rank)
+            if nr:
+                got_r = ws.resid(T)[r0:r0 + nr].float()
+                er = ((got_r - want_r[r0:r0 + nr].float()).norm() / want_r[r0:r0 + nr].float().norm()).item()
+                assert er < 1e-2, (K, T, mode, rep, "resid", er)
+            got_n = ws.normed(T).float()
+            assert torch.isfinite(got_n).all(), (K, T, mode, rep, "normed rows not written")
+            en = ((got_n - want_n).norm() / want_n.norm()).item()
+            assert en < 2e-2, (K, T, mode, rep, "normed", en)
+            parity ^= 1
+
+
 def _timeout_check(rank, world):
     import time
     import torch.distributed as dist
@@ -169,67 +220,123 @@ def _timeout_check(rank, world):
     assert torch.allclose(ws.resid(8).float(), torch.full((8, H), float(world), device=dev))
 
 
-def _tp_logits(rank, world):
+def _tp_logits(rank, world, preset="small", layers=0, nvls=False):
+    """Prefill of one prompt, then decode steps of a 3-session batch (the decode steps take the
+    fused GEMM + all-reduce path at TP>1), teacher-forced with the TP=1 run's greedy tokens: every
+    step's full-vocabulary logits at TP=world against TP=1, and each TP=world token equal to the
+    argmax of its own logits."""
     import torch.distributed as dist
     from mesh_b200.config import EngineConfig, get_preset
     from mesh_b200.models.llama import KVPool, LlamaRunner, StepMeta
+    from mesh_b200.models.sharding import even_split
     from mesh_b200.models.weights import synthetic_device_weights
     dev = torch.device("cuda", rank)
-    cfg = get_preset("small")
-    ecfg = EngineConfig(max_seq_len=256)
-    prompt = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(5)).tolist()
+    cfg = get_preset(preset)
+    if layers:
+        cfg = cfg.replace(num_layers=layers)
+    if cfg.num_kv_heads % world:
+        return f"{preset} has {cfg.num_kv_heads} KV heads, not divisible over {world} ranks"
+    ecfg = EngineConfig(max_seq_len=256, nvls=nvls)
+    gen = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (40, 17, 33)]
+    steps = 4
 
-    def run(world_, rank_, group):
+    def run(world_, rank_, group, forced=None):
         w = synthetic_device_weights(cfg, rank_, world_, seed=9, device=dev, norm_noise=True)
-        kv = KVPool(cfg, w.layout.local_kv_heads, 16, 16, dev)
+        kv = KVPool(cfg, w.layout.local_kv_heads, 64, 16, dev)
         r = LlamaRunner(w, ecfg, kv, dev, group=group, max_tokens=256)
         r.keep_logits = True
-        T = len(prompt)
-        bt = torch.zeros(1, 8, dtype=torch.int32, device=dev)
-        bt[0, :3] = torch.tensor([1, 2, 3])
-        pos = torch.arange(T, device=dev)
-        m = StepMeta(ids=torch.tensor(prompt, dtype=torch.int32, device=dev), pos=pos.int(),
-                     slot=(bt[0, pos // 16].long() * 16 + pos % 16), block_tables=bt,
-                     seq_lens=torch.tensor([T], dtype=torch.int32, device=dev),
-                     cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev),
-                     last_idx=torch.tensor([T - 1], device=dev), max_q_len=T, decode=False)
-        ids = r.forward(m)
+        B = len(prompts)
+        bt = torch.zeros(B, 8, dtype=torch.int32, device=dev)
+        for b in range(B):
+            bt[b, :4] = torch.arange(1 + 4 * b, 5 + 4 * b)
+        logits, toks, nxt = [], [], []
+        for b, p in enumerate(prompts):
+            T = len(p)
+            pos = torch.arange(T, device=dev)
+            m = StepMeta(ids=torch.tensor(p, dtype=torch.int32, device=dev), pos=pos.int(),
+                         slot=(bt[b, pos // 16].long() * 16 + pos % 16), block_tables=bt[b:b + 1],
+                         seq_lens=torch.tensor([T], dtype=torch.int32, device=dev),
+                         cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev),
+                         last_idx=torch.tensor([T - 1], device=dev), max_q_len=T, decode=False)
+            ids = r.forward(m)
+            logits.append(r.last_logits[0].float().clone())
+            nxt.append(int(ids[0]))
+        toks.append(list(nxt))
+        for st in range(steps):
+            feed = forced[st] if forced is not None else nxt
+            lens = [len(p) + st for p in prompts]
+            pos = torch.tensor(lens, device=dev)
+            m = StepMeta(ids=torch.tensor(feed, dtype=torch.int32, device=dev), pos=pos.int(),
+                         slot=(bt[torch.arange(B, device=dev), pos // 16].long() * 16 + pos % 16),
+                         block_tables=bt, seq_lens=(pos + 1).int(), max_q_len=128, decode=True)
+            ids = r.forward(m)
+            for b in range(B):
+                logits.append(r.last_logits[b].float().clone())
+            nxt = ids.tolist()
+            toks.append(list(nxt))
         torch.cuda.synchronize()
-        return r.last_logits[0].float(), int(ids[0]), w
+        return logits, toks
 
-    full, id1, _ = run(1, 0, None)
-    part, id2, w2 = run(world, rank, dist.group.WORLD)
-    parts = [torch.empty(n, device=dev) for n in
-             [__import__("mesh_b200.models.sharding", fromlist=["x"]).even_split(cfg.vocab_size, world, r)[1]
-              for r in range(world)]]
-    dist.all_gather(parts, part.contiguous())
-    tp = torch.cat(parts)
-    err = ((tp - full).norm() / full.norm()).item()
-    assert err < 3e-2, err
-    assert id2 == int(tp.argmax())
-
-
-@pytest.fixture(autouse=True)
-def _need_gpus():
-    if torch.cuda.device_count() < NEED:
-        pytest.skip(f"needs {NEED} GPUs")
+    full, toks1 = run(1, 0, None)
+    part, toksn = run(world, rank, dist.group.WORLD, forced=toks1)
+    sizes = [even_split(cfg.vocab_size, world, r)[1] for r in range(world)]
+    for i, (f, p) in enumerate(zip(full, part)):
+        parts = [torch.empty(n, device=dev) for n in sizes]
+        dist.all_gather(parts, p.contiguous())
+        tp = torch.cat(parts)
+        err = ((tp - f).norm() / f.norm()).item()
+        assert err < 3e-2, (i, err)
+        step, b = (0, i) if i < len(prompts) else (1 + (i - len(prompts)) // len(prompts), (i - len(prompts)) % 3)
+        assert toksn[step][b] == int(tp.argmax()), (i, toksn[step][b], int(tp.argmax()))
 
 
-def test_fused_allreduce_norm_2gpu():
-    _run(_ar_check, 2)
+def _need(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
 
 
-def test_fused_allreduce_norm_nvls_2gpu():
-    _run(_ar_check, 2, True)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_allreduce_norm(world):
+    _need(world)
+    _run(_ar_check, world)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_fused_allreduce_norm_nvls(world):
+    _need(world)
+    _run(_ar_check, world, True)
 
 
 def test_fused_gemm_reduce_scatter_push_2gpu():
+    _need(2)
     _run(_push_check, 2)
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_gemm_allreduce_norm_one_launch(world):
+    _need(world)
+    _run(_gemm_ar_check, world)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_gemm_allreduce_norm_one_launch_nvls(world):
+    _need(world)
+    _run(_gemm_ar_check, world, True)
+
+
 def test_allreduce_bounded_wait_reports_timeout_2gpu():
+    _need(2)
     _run(_timeout_check, 2)
 
 
 def test_tp2_logits_match_tp1():
+    _need(2)
     _run(_tp_logits, 2)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tpn_llama3_shape_logits_match_tp1(world):
+    """Llama-3-8B-shaped (2 layers) at TP=4/8, NVLS on at 8 ranks as in serving."""
+    _need(world)
+    _run(_tp_logits, world, "llama3-8b", 2, world >= 8)
