@@ -7,7 +7,8 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int
                   const c10::optional<at::Tensor>& trace, const std::vector<int64_t>& push);
 void gemm_allreduce_norm(const at::Tensor& w, const at::Tensor& x, at::Tensor& part, const std::vector<int64_t>& push,
                          const std::vector<int64_t>& cfg, const at::Tensor& gamma, double eps, at::Tensor& epoch,
-                         int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err);
+                         int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                         const c10::optional<at::Tensor>& trace);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, bool trans, int64_t device);
 void gemm_qkv_rope(const at::Tensor& w, const at::Tensor& x, at::Tensor& q_out, const at::Tensor& pos,
                    const at::Tensor& slot, const at::Tensor& cos_t, const at::Tensor& sin_t, at::Tensor& kcache,
@@ -53,7 +54,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("push") = std::vector<int64_t>{});
   m.def("gemm_qkv_rope", &mesh::gemm_qkv_rope, "decode qkv GEMM with RoPE and the paged KV write in the epilogue");
   m.def("gemm_allreduce_norm", &mesh::gemm_allreduce_norm,
-        "decode GEMM with the tensor-parallel all-reduce, residual add, RMSNorm and all-gather fused in");
+        "decode GEMM with the tensor-parallel all-reduce, residual add, RMSNorm and all-gather fused in",
+        py::arg("w"), py::arg("x"), py::arg("part"), py::arg("push"), py::arg("cfg"), py::arg("gamma"), py::arg("eps"),
+        py::arg("epoch"), py::arg("mode"), py::arg("workspace"), py::arg("counters"), py::arg("err"),
+        py::arg("trace") = py::none());
   m.def("gemm_plan", &mesh::gemm_plan, "tile plan [bn, workspace_floats, stream-K tiles, stages, grid, dp_tiles, sk_iters]");
   m.def("add_rmsnorm", &mesh::add_rmsnorm, "resid += delta; normed = rmsnorm(resid) * gamma");
   m.def("rope_kv_write", &mesh::rope_kv_write, "RoPE on q/k + paged KV write");

@@ -55,6 +55,8 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: far above any legal w
 // over the ranks' pushed partials, adds the residual, applies RMSNorm and writes the normed rows
 // into every rank (NVLS multicast store, or one peer store per rank), all inside the same launch.
 constexpr int AR_TAIL_MAX_RANKS = 8;
+// %globaltimer stamps per CTA: 0-15 GEMM phases, 16-21 the fused all-reduce tail
+constexpr int TRACE_SLOTS = 32;
 struct ArTail {
   int on;
   int rank, world, T, H, t_max;
@@ -99,7 +101,7 @@ struct GemmParams {
   int* err;
   uint32_t idesc;
   uint32_t tmem_cols;
-  unsigned long long* trace;  // optional [grid][16] %globaltimer stamps (nullptr: off)
+  unsigned long long* trace;  // optional [grid][TRACE_SLOTS] %globaltimer stamps (nullptr: off)
   // Fused reduce-scatter: instead of `out`, bf16 rows go to slot `my_rank` of the destination
   // rank's symmetric buffer over NVLink (1: each token row to its owner rank, 2: to every rank).
   int push_mode, my_rank, world, push_rows;
@@ -1122,14 +1124,17 @@ __device__ __forceinline__ void ar_tail_row(const ArTail& a, long row, int et, v
   }
 }
 
-__device__ __forceinline__ void ar_tail(const GemmParams& p, const Smem& s, int et) {
+__device__ __forceinline__ void ar_tail(const GemmParams& p, const Smem& s, int et, unsigned long long* trace) {
   const ArTail& a = p.ar;
+  const bool tr = trace != nullptr && et == 0;
+  if (tr) trace[16] = globaltimer_ns();
   volatile uint32_t* s_e = reinterpret_cast<volatile uint32_t*>(s.epi);  // [0] epoch, [1] ok
   volatile float* red = reinterpret_cast<volatile float*>(s.epi) + 4;  // [4] sum-of-squares partials
   if (et == 0) s_e[0] = *a.epoch + 1u;
   named_bar_sync(1, 128);
   const uint32_t e = s_e[0];
   ar_arrive(a, 0, e, gridDim.x, et);
+  if (tr) trace[17] = globaltimer_ns();
   const int base = a.T / a.world, extra = a.T % a.world;
   const long r0 = (long)a.rank * base + min(a.rank, extra);
   const int nrows = base + (a.rank < extra ? 1 : 0);
@@ -1137,21 +1142,25 @@ __device__ __forceinline__ void ar_tail(const GemmParams& p, const Smem& s, int 
   volatile int* s_ok = reinterpret_cast<volatile int*>(s_e + 1);
   if ((int)blockIdx.x < nred) {
     if (ar_wait(p, 0, e, et, s_ok)) {
+      if (tr) trace[18] = globaltimer_ns();
       for (long row = r0 + blockIdx.x; row < r0 + nrows; row += gridDim.x) {
         if (a.H <= 128 * 8 * 4)
           ar_tail_row<4>(a, row, et, red);
         else
           ar_tail_row<8>(a, row, et, red);
       }
+      if (tr) trace[19] = globaltimer_ns();
     }
     __threadfence_system();  // this thread's normed stores (peer or multicast) before the signal
     ar_arrive(a, 1, e, nred, et);
+    if (tr) trace[20] = globaltimer_ns();
   } else if (nred == 0 && blockIdx.x == 0 && et == 0) {
     fence_acq_rel_sys();
     for (int d = 0; d < a.world; ++d) st_release_sys(ar_flag(a, d, 1, a.rank), e);
   }
   if (blockIdx.x == 0) {
     ar_wait(p, 1, e, et, s_ok);
+    if (tr) trace[21] = globaltimer_ns();
     if (et == 0) *a.epoch = e;
   }
 }
@@ -1196,7 +1205,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = *s.tmem_base;
   volatile int* abort_flag = s.abort_flag;
   if (TRANS && p.ck > 1) cluster_arrive_relaxed();  // waited on before any remote shared-memory access
-  unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * 16 : nullptr;
+  unsigned long long* trace = p.trace ? p.trace + (size_t)blockIdx.x * TRACE_SLOTS : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer_ns();
   // the next kernel may start its prologue on SMs this grid frees up
   griddep_launch_dependents();
@@ -1567,7 +1576,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   if constexpr (TRANS && EPI == EPI_STORE_BF16) {
     // fused all-reduce tail: TMEM is already released, so cross-GPU waits hold no tensor memory
-    if (p.ar.on && warp >= 2) ar_tail(p, s, threadIdx.x - 64);
+    if (p.ar.on && warp >= 2) ar_tail(p, s, threadIdx.x - 64, trace);
   }
   if (trace && threadIdx.x == 0) trace[7] = globaltimer_ns();
 }
@@ -1902,7 +1911,8 @@ static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
     p.ar.on = 1;
   }
   if (trace.has_value()) {
-    TORCH_CHECK(trace->numel() >= (int64_t)pl.grid * 16 && trace->scalar_type() == at::kLong, "gemm trace buffer");
+    TORCH_CHECK(trace->numel() >= (int64_t)pl.grid * TRACE_SLOTS && trace->scalar_type() == at::kLong,
+                "gemm trace buffer: int64 [grid * 32]");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
   p.err = err.data_ptr<int>();
@@ -1980,7 +1990,8 @@ void gemm_qkv_rope(const at::Tensor& w, const at::Tensor& x, at::Tensor& q_out, 
 //         workspace base of each rank...]; `part` is this rank's local push slot (shape checks only).
 void gemm_allreduce_norm(const at::Tensor& w, const at::Tensor& x, at::Tensor& part, const std::vector<int64_t>& push,
                          const std::vector<int64_t>& cfg, const at::Tensor& gamma, double eps, at::Tensor& epoch,
-                         int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err) {
+                         int64_t mode, at::Tensor& workspace, at::Tensor& counters, at::Tensor& err,
+                         const c10::optional<at::Tensor>& trace) {
   const int64_t T = x.size(0), H = w.size(0);
   TORCH_CHECK(push.size() >= 6 && push[0] == 1 && push[3] == T && push[5] == H, "gemm_allreduce_norm: push table");
   const int world = (int)push[2];
@@ -2009,7 +2020,7 @@ void gemm_allreduce_norm(const at::Tensor& w, const at::Tensor& x, at::Tensor& p
   a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
   a.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr());
   a.eps = (float)eps;
-  gemm_impl(w, x, part, EPI_STORE_BF16, true, 0, mode, workspace, counters, err, c10::nullopt, push, nullptr, &a);
+  gemm_impl(w, x, part, EPI_STORE_BF16, true, 0, mode, workspace, counters, err, trace, push, nullptr, &a);
 }
 
 // [bn, workspace floats, stream-K tiles, stages, grid, dp_tiles, sk_iters, cluster split]

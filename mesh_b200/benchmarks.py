@@ -4,6 +4,7 @@
     torchrun ... -m mesh_b200.benchmarks prefill      # 2k/8k/32k single-sequence prefill (TTFT)
     torchrun ... -m mesh_b200.benchmarks allreduce    # fused AR+norm vs NCCL vs host ring
     torchrun ... -m mesh_b200.benchmarks serve70b     # 70B TP=8, 256 sessions, 10% KV handoff
+    torchrun ... -m mesh_b200.benchmarks gemmar       # decode GEMM + all-reduce: separate vs one launch
 
 Every GPU number is timed with CUDA events on the launching stream after warm-up and reported as
 the max over ranks; rank 0 prints one JSON line per measurement.
@@ -270,6 +271,97 @@ def allreduce(args):
     mdist.shutdown()
 
 
+# ------------------------------------------------------------------------------------ GEMM + all-reduce
+def gemmar(args):
+    """Decode o_proj / down_proj followed by the TP all-reduce + residual + RMSNorm: per-call device
+    time of (a) the GEMM alone, (b) the GEMM then the separate all-reduce kernel, (c) both in one
+    launch (``gemm_allreduce_norm``), each captured in a CUDA graph of 20 calls with weights rotated
+    past L2, max over ranks; plus the fused launch's per-phase timeline from %globaltimer stamps
+    (medians over CTAs, us after the first CTA started)."""
+    di, dist, torch = _dist()
+    from . import ops
+    from .config import get_preset
+    from .models.sharding import shard_layout
+    from .models.weights import GU_BLOCK, pad_to
+    from .parallel.symm import SymmWorkspace
+    cfg = get_preset(args.model)
+    dev = di.device
+    lay = shard_layout(cfg, di.rank, di.world)
+    H = cfg.hidden_dim
+    shapes = [("o_proj", lay.q_cols), ("down", pad_to(lay.mlp_cols, GU_BLOCK))]
+    ws = SymmWorkspace(max(args.tokens), H, dev, multicast=not args.no_nvls)
+    mc = bool(ws.mc_base) and di.world >= 8
+    gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    side = torch.cuda.Stream(dev)
+    iters = 20
+
+    def graphed(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        ops.scratch(dev).check("gemmar warm-up")
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                for i in range(iters):
+                    fn(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(3):
+            g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        ops.scratch(dev).check("gemmar")
+        del g
+        return round(_max_over_ranks(s.elapsed_time(e) * 1e3 / (3 * iters), dist, torch, dev), 2)
+
+    for name, K in shapes:
+        nc = max(2, min(32, (2 * 126 * 2 ** 20) // (H * K * 2) + 1))
+        wts = [torch.randn(H, K, device=dev).mul_(0.02).to(torch.bfloat16) for _ in range(nc)]
+        for T in args.tokens:
+            x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+            ws.resid(T).normal_()
+            row = {"op": name, "T": T, "K": K, "H": H, "world": di.world, "nvls": mc}
+            row["gemm_us"] = graphed(lambda i: ops.linear(x, wts[i % nc], out=ws.partial(i & 1, T)))
+            two = T * H * 2 * (di.world - 1) > (8 << 20) and di.world > 2
+            row["gemm_then_ar_us"] = graphed(lambda i: (
+                ops.linear(x, wts[i % nc], out=ws.partial(i & 1, T)),
+                ws.fused_allreduce_norm(T, i & 1, gamma, 1e-5, two_shot=two, multicast=mc)))
+            row["fused_us"] = graphed(lambda i: ws.gemm_allreduce_norm(x, wts[i % nc], i & 1, gamma, 1e-5,
+                                                                       multicast=mc))
+            plan = ops.ext().gemm_plan(H, T, K, ops.EPI_STORE_BF16, True, dev.index)
+            tr = torch.zeros(160 * 32, dtype=torch.int64, device=dev)
+            dist.barrier()
+            ws.gemm_allreduce_norm(x, wts[0], 0, gamma, 1e-5, multicast=mc, trace=tr)
+            torch.cuda.synchronize()
+            t = tr.view(-1, 32)[: plan[4]].cpu()
+            t0 = int(t[:, 0].min())
+            rel = lambda c, sel=None: ((t[:, c] if sel is None else t[sel, c]).double() - t0) / 1e3  # noqa: E731
+            med = lambda v: round(float(v.median()), 2) if len(v) else None  # noqa: E731
+            red = t[:, 18] > 0
+            row["plan"] = {"bn": plan[0], "grid": plan[4], "ck": plan[7], "dp_tiles": plan[5]}
+            row["timeline_us"] = {
+                "cta_start_max": round(float(rel(0).max()), 2), "griddep_passed": med(rel(1)),
+                "mma_done_max": round(float(rel(4).max()), 2), "tail_start_med": med(rel(16)),
+                "tail_start_max": round(float(rel(16).max()), 2), "phase0_arrived_max": round(float(rel(17).max()), 2),
+                "reducers": int(red.sum()), "phase0_passed_med": med(rel(18, red)), "rows_done_med": med(rel(19, red)),
+                "phase1_arrived_max": round(float(rel(20, red).max()), 2) if red.any() else None,
+                "phase1_passed_cta0": round(float(rel(21)[0]), 2), "exit_max": round(float(rel(7).max()), 2)}
+            if di.rank == 0:
+                print(json.dumps(row), flush=True)
+        del wts
+    del ws
+    from .parallel import dist as mdist
+    mdist.shutdown()
+
+
 # ------------------------------------------------------------------------------------ 70B serving
 def serve70b(args):
     """256 sessions, prompts U[128,2048], 256 output tokens; after half the decode steps 10% of
@@ -359,6 +451,10 @@ def main():
     c5.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 4096, 8192])
     c5.add_argument("--hidden", type=int, nargs="+", default=[4096, 8192])
     c5.add_argument("--no-host-ring", action="store_true")
+    c6 = sub.add_parser("gemmar")
+    c6.add_argument("--model", default="llama3-8b")
+    c6.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 128])
+    c6.add_argument("--no-nvls", action="store_true")
     c4 = sub.add_parser("serve70b")
     c4.add_argument("--model", default="llama3-70b")
     c4.add_argument("--sessions", type=int, default=256)
@@ -367,7 +463,8 @@ def main():
     c4.add_argument("--handoff", type=float, default=0.1)
     c4.add_argument("--layers", type=int, default=0)
     a = ap.parse_args()
-    {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b}[a.cmd](a)
+    {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b,
+     "gemmar": gemmar}[a.cmd](a)
 
 
 if __name__ == "__main__":

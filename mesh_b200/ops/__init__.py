@@ -132,7 +132,8 @@ _PLANS = {}
 
 
 def gemm_allreduce_norm(w: torch.Tensor, x: torch.Tensor, part_view: torch.Tensor, push: list, cfg: list,
-                        gamma: torch.Tensor, eps: float, epoch: torch.Tensor, mode: int = 0):
+                        gamma: torch.Tensor, eps: float, epoch: torch.Tensor, mode: int = 0,
+                        trace: Optional[torch.Tensor] = None):
     """Swap-AB decode GEMM x @ w.T whose epilogue pushes partial rows to their owner ranks, with the
     tensor-parallel reduction, residual add, RMSNorm and all-gather of the normed rows in the same
     launch (``parallel.symm.SymmWorkspace.gemm_allreduce_norm`` builds the tables)."""
@@ -144,7 +145,8 @@ def gemm_allreduce_norm(w: torch.Tensor, x: torch.Tensor, part_view: torch.Tenso
         plan = _PLANS[key] = ext().gemm_plan(M, N, K, EPI_STORE_BF16, True, x.device.index)
     if plan[2] > 0:
         s.ensure_gemm(plan[1], plan[2])
-    ext().gemm_allreduce_norm(w, x, part_view, push, cfg, gamma, eps, epoch, mode, s.gemm_ws, s.gemm_counters, s.err)
+    ext().gemm_allreduce_norm(w, x, part_view, push, cfg, gamma, eps, epoch, mode, s.gemm_ws, s.gemm_counters, s.err,
+                              trace)
     _count()
 
 

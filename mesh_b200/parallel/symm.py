@@ -166,7 +166,8 @@ class SymmWorkspace:
         ops._count()
 
     def gemm_allreduce_norm(self, x: torch.Tensor, w: torch.Tensor, parity: int, gamma: torch.Tensor, eps: float,
-                            timeout_s: float = 5.0, mode: int = 0, multicast: bool = True):
+                            timeout_s: float = 5.0, mode: int = 0, multicast: bool = True,
+                            trace: Optional[torch.Tensor] = None):
         """One launch: partial = x @ w.T on this rank, summed over the TP group, added to ``resid``
         and RMS-normalised into ``normed`` on every rank. Decode-sized T (swap-AB GEMM). Each rank
         keeps only the ``resid`` rows it owns current (the same rows in every call with this T);
@@ -180,7 +181,7 @@ class SymmWorkspace:
         cfg = [L.t_max, L.off_gflags, L.off_gcount, off, L.off_resid, L.off_normed,
                self.mc_base if multicast else 0, int(timeout_s * 1e9)] + self._bases
         local = self.view(off + self.rank * L.t_max * L.hidden * 2, T)
-        ops.gemm_allreduce_norm(w, x, local, push, cfg, gamma, eps, self.gepoch, mode)
+        ops.gemm_allreduce_norm(w, x, local, push, cfg, gamma, eps, self.gepoch, mode, trace)
 
     def reset(self):
         """Collective: zero the flags and epoch counters on every rank. Needed after a timed-out

@@ -95,11 +95,11 @@ def trace_gemms(cfg, s, T, modes=(0, 1)):
         xin = torch.randn(T, K, device=dev).to(torch.bfloat16)
         out = torch.empty(T, N // 2 if epi == 2 else N, device=dev, dtype=torch.bfloat16)
         for mode in modes:
-            tr = torch.zeros(148 * 16, dtype=torch.int64, device=dev)
+            tr = torch.zeros(148 * 32, dtype=torch.int64, device=dev)
             for _ in range(3):
                 ops.gemm(w, xin, out, epi, trans=True, trace=tr, mode=mode)
             torch.cuda.synchronize()
-            t = tr.view(-1, 16).cpu()
+            t = tr.view(-1, 32).cpu()
             t = t[t[:, 0] > 0]
             t0 = t[:, 0].min()
             rel = (t - t0).double() / 1e3

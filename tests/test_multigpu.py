@@ -1,4 +1,4 @@
-"""Tensor-parallel paths on 2, 4 and 8 GPUs (and the fused GEMM + all-reduce launch on one), run as
+"""Tensor-parallel paths on 2, 4 and 8 GPUs, run as
 spawned child processes (NCCL for plumbing with its NVLS off; the fused kernels on plain peer loads,
 except the tests that check their NVLS multicast path).
 
@@ -313,7 +313,7 @@ def test_fused_gemm_reduce_scatter_push_2gpu():
     _run(_push_check, 2)
 
 
-@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_gemm_allreduce_norm_one_launch(world):
     _need(world)
     _run(_gemm_ar_check, world)
