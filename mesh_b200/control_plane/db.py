@@ -73,7 +73,7 @@ CREATE TABLE IF NOT EXISTS inference_regroup_events (
   id INTEGER PRIMARY KEY AUTOINCREMENT, job_id TEXT, session_id TEXT, decision TEXT, details TEXT, created_at REAL);
 CREATE TABLE IF NOT EXISTS inference_session_checkpoints (
   job_id TEXT NOT NULL, session_id TEXT NOT NULL, payload BLOB NOT NULL, token_index INTEGER, created_at REAL,
-  PRIMARY KEY (job_id, session_id));
+  source_device_id TEXT, PRIMARY KEY (job_id, session_id));
 CREATE TABLE IF NOT EXISTS inference_session_kv_residency (
   session_id TEXT NOT NULL, device_id TEXT NOT NULL, seq_len INTEGER, updated_at REAL,
   PRIMARY KEY (session_id, device_id));

@@ -6,18 +6,23 @@ Behaviour restated from the reference control plane (``control-plane/src``):
 * ring topology: sequential positions, weighted GQA-aligned column ranges, neighbours, version
   counter, handoffs and callbacks (``services/ring_manager.rs:140-1091``,
   ``services/topology_notifier.rs``);
-* execution planning: prefill and decode execution groups over the ring's TP members, segments
-  ``segment-<session>-prefill/-decode``, co-located KV (``services/planner.rs:49-372``);
+* execution planning: prefill and decode members chosen separately under the model's execution
+  layout rules and scored per runtime mode (``planner.py``, ``services/planner.rs:49-372``); a
+  decode group that differs from the prefill group receives the KV by checkpoint handoff;
 * submit: tokenize, quote + reserve credits, persist job / session / groups / assignments and a
   decode queue entry ``blocked_on_prefill`` in one transaction (``api/inference.rs:383-765``);
-* claim: in-flight prefill assignments first, then decode cohorts for ready sessions, 60 s leases
-  (``api/inference.rs:4567-4925``, ``services/scheduler.rs:119-197``); renew / release leases;
+* claim: the claim-time scheduler (``scheduler.py``) orders this worker's prefill assignments and
+  decode-queue entries (in-flight prefill groups first, blocked reasons, soft caps), then a
+  decode claim leases the cohort of runnable sessions, 60 s leases (``api/inference.rs:4567-4925``,
+  ``services/scheduler.rs:119-197``); renew / release leases;
 * progress: PrefillComplete moves the queue entry to ``ready`` (co-located) or
   ``blocked_on_transfer`` (handoff) (``api/inference.rs:5782-6412``);
 * result: completion, settlement through the credit policy, ledger events (``:5320-5781``);
-* failover: prefill loss -> fail and release credits; decode loss -> replace with an idle ring
-  member, shrink to the survivors when they still cover every column, else fail; resume mode
-  from the available checkpoint (``services/failover.rs:174-700``);
+* failover: the failover engine (``failover.py``): prefill loss -> fail and release credits;
+  decode loss -> the decode group re-planned on the live ring, else the survivors that still cover
+  the columns; resume immediately, after a live KV handoff or after a checkpoint transfer
+  (``services/failover.rs:174-700``); terminal sessions and orphaned leases are cleaned up
+  (``:2158-2312``);
 * presence: devices silent for 15 s become stale and trigger failover
   (``services/presence.rs:12-96``).
 """
@@ -31,8 +36,13 @@ import uuid
 from typing import Dict, List, Optional, Tuple
 
 from ..config import ModelConfig, PRESETS
+from . import failover as fo
+from . import planner as planner_mod
 from . import policy
+from . import scheduler as sched
 from .db import Database, dumps, loads
+from .layout import LayoutError, Member, ModelManifest
+from .provider import contract_for_device
 
 ASSIGNMENT_LEASE_SECS = 60.0
 DECODE_QUEUE_STATUSES = ("blocked_on_prefill", "blocked_on_transfer", "ready", "leased", "active", "completed",
@@ -87,6 +97,40 @@ class ControlPlane:
             cfg = PRESETS[model_id]
             return cfg, cfg.param_count() * 2
         raise NotFound(f"unknown model {model_id}")
+
+    def manifest(self, model_id: str) -> ModelManifest:
+        """The planning view of a model: ``model.json`` (with its ``execution_layout`` rules) from
+        the model store, else the attention geometry of the built-in preset."""
+        if self.model_store:
+            p = os.path.join(self.model_store, model_id, "model.json")
+            if os.path.exists(p):
+                m = json.load(open(p))
+                m.setdefault("model_id", model_id)
+                m.setdefault("total_model_bytes", self.model_config(model_id)[1])
+                try:
+                    return ModelManifest.from_json(m)
+                except LayoutError as e:
+                    raise ApiError(str(e)) from e
+        cfg, total = self.model_config(model_id)
+        return ModelManifest(model_id, cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads, total, cfg.num_layers)
+
+    def _members(self, network_id: str, model_id: str, exclude=()) -> List[Member]:
+        """Online ring members of a model as planner members (contract from the device's
+        advertised capabilities, capacity units from its tier)."""
+        rows = self.db.query(
+            "SELECT m.device_id, m.position, m.column_start, m.column_end, m.contributed_memory, d.tier, d.provider, "
+            "d.capabilities, d.status, d.tensor_plane_addr FROM ring_members m JOIN devices d ON d.device_id=m.device_id "
+            "WHERE m.network_id=? AND m.model_id=? AND m.status='active' ORDER BY m.position", (network_id, model_id))
+        out = []
+        for r in rows:
+            if r["device_id"] in exclude or r["status"] != "online" or r["column_end"] <= r["column_start"]:
+                continue
+            out.append(Member(r["device_id"], r["position"], r["column_start"], r["column_end"],
+                              contributed_memory=r["contributed_memory"] or 0,
+                              assigned_capacity_units=policy.TIER_CAPACITY_UNITS.get(r["tier"] or "tier2", 4),
+                              backend_contract=contract_for_device(r["provider"] or "cpu", loads(r["capabilities"], {})),
+                              listen_addrs=["dataplane://" + (r["tensor_plane_addr"] or r["device_id"])]))
+        return out
 
     def tokenize(self, model_id: str, prompt: str) -> List[int]:
         """Tokenizer of the model store when present (``model_assets.rs:871-891``), else UTF-8 bytes."""
@@ -288,24 +332,18 @@ class ControlPlane:
 
     # ------------------------------------------------------------------------------------ inference
     def plan(self, network_id: str, model_id: str, session_id: str) -> dict:
+        """Prefill and decode groups for a new session (``planner.plan``); Conflict when the live
+        ring cannot form a legal group."""
         topo = self.topology(network_id, model_id)
         if not topo["stable"]:
             raise Conflict("ring is not stable: no full column coverage by online workers")
-        members = [{"device_id": w["device_id"], "worker_position": w["position"], "total_workers": topo["total_workers"],
-                    "shard_column_start": w["column_start"], "shard_column_end": w["column_end"]}
-                   for w in topo["workers"]]
-        pid = _uid()
-        groups = [{"group_id": f"group-{pid}-prefill", "phase": "prefill", "members": members},
-                  {"group_id": f"group-{pid}-decode", "phase": "decode", "members": members}]
-        segs = [{"segment_id": f"segment-{session_id}-prefill", "phase": "prefill",
-                 "execution_group_id": groups[0]["group_id"], "session_id": session_id,
-                 "participant_device_ids": [m["device_id"] for m in members]},
-                {"segment_id": f"segment-{session_id}-decode", "phase": "decode",
-                 "execution_group_id": groups[1]["group_id"], "session_id": session_id,
-                 "participant_device_ids": [m["device_id"] for m in members]}]
-        return {"plan_id": pid, "model_id": model_id, "execution_groups": groups, "segments": segs,
-                "kv_owner_device_id": members[0]["device_id"], "kv_transfer_policy": "co_located",
-                "topology_version": topo["version"]}
+        try:
+            p = planner_mod.plan(self.manifest(model_id), self._members(network_id, model_id))
+        except (planner_mod.PlanningError, LayoutError) as e:
+            raise Conflict(str(e)) from e
+        out = p.to_json(model_id, session_id)
+        out["topology_version"] = topo["version"]
+        return out
 
     def submit_inference(self, network_id: str, model_id: str, prompt: Optional[str] = None,
                          prompt_tokens: Optional[List[int]] = None, max_tokens: int = 100, temperature: float = 0.7,
@@ -333,13 +371,13 @@ class ControlPlane:
             for g in plan["execution_groups"]:
                 c.execute("INSERT INTO inference_serving_groups VALUES (?,?,?,?,?,'planned')",
                           (g["group_id"], job_id, session_id, g["phase"], dumps([m["device_id"] for m in g["members"]])))
-            for m in plan["execution_groups"][0]["members"]:
+            for i, m in enumerate(plan["execution_groups"][0]["members"]):
                 c.execute("""INSERT INTO inference_job_assignments (assignment_id, job_id, session_id, device_id, phase,
                              segment_id, group_id, status, shard_column_start, shard_column_end, worker_position,
                              total_workers, created_at, updated_at) VALUES (?,?,?,?,'prefill',?,?,'pending',?,?,?,?,?,?)""",
                           (_uid(), job_id, session_id, m["device_id"], plan["segments"][0]["segment_id"],
                            plan["execution_groups"][0]["group_id"], m["shard_column_start"], m["shard_column_end"],
-                           m["worker_position"], m["total_workers"], now, now))
+                           i, m["total_workers"], now, now))
             c.execute("INSERT INTO inference_decode_queue VALUES (?,?,?,'blocked_on_prefill',NULL,NULL,NULL,0,0,0,?)",
                       (session_id, job_id, network_id, now))
             self._ledger(c, network_id, submitter_device_id, job_id, "credits_reserved", quote["total_credits"], quote)
@@ -352,22 +390,125 @@ class ControlPlane:
     def _lease(self) -> Tuple[str, float]:
         return _uid(), _now() + ASSIGNMENT_LEASE_SECS
 
-    def claim(self, device_id: str, max_decode_sessions: int = 64) -> dict:
-        """Claim-time scheduling: in-flight prefill first, then a decode cohort of ready sessions
-        whose decode group contains this device (one lease per session)."""
+    @staticmethod
+    def _iso(t: Optional[float]) -> str:
+        import datetime as _dt
+        return _dt.datetime.fromtimestamp(t or 0.0, _dt.timezone.utc).strftime("%Y-%m-%dT%H:%M:%S.%fZ")
+
+    def _claim_candidates(self, c, device_id: str) -> Tuple[List[sched.Candidate], dict, sched.Snapshot]:
+        """The scheduler's view of what ``device_id`` could take: its pending prefill assignments
+        and the decode-queue entries whose decode group contains it, with group and cohort state."""
+        iso = self._iso
+        cands: List[sched.Candidate] = []
+        rows = {}
+        inflight_by_model: Dict[str, set] = {}
+        for r in c.execute("SELECT a.job_id, j.model_id FROM inference_job_assignments a JOIN inference_jobs j ON "
+                           "j.job_id=a.job_id WHERE a.phase='prefill' AND a.status IN ('leased','acked') AND "
+                           "j.status IN ('pending','running')").fetchall():
+            inflight_by_model.setdefault(r["model_id"], set()).add(r["job_id"])
+        for r in c.execute("""SELECT a.*, j.prompt_tokens, j.max_tokens, j.temperature, j.top_p, j.model_id, j.network_id,
+                              j.runtime_mode, j.submitter_device_id, j.created_at AS job_created FROM
+                              inference_job_assignments a JOIN inference_jobs j ON j.job_id=a.job_id WHERE a.device_id=?
+                              AND a.phase='prefill' AND a.status='pending' AND j.status IN ('pending','running')""",
+                           (device_id,)).fetchall():
+            r = dict(r)
+            st = [x["status"] for x in c.execute("SELECT status FROM inference_job_assignments WHERE job_id=? AND "
+                                                 "phase='prefill'", (r["job_id"],)).fetchall()]
+            others = inflight_by_model.get(r["model_id"], set()) - {r["job_id"]}
+            cands.append(sched.Candidate(
+                assignment_id=r["assignment_id"], job_id=r["job_id"], session_id=r["session_id"], phase="prefill",
+                group_status="prefill_member", model_id=r["model_id"], ring_position=r["worker_position"] or 0,
+                runtime_mode=r["runtime_mode"] or "throughput_first", submitted_by_device_id=r["submitter_device_id"] or "",
+                created_at=iso(r["job_created"]), assigned_at=iso(r["created_at"]),
+                prefill_group_total_members=len(st),
+                prefill_group_leased_members=sum(1 for x in st if x in ("leased", "acked")),
+                prefill_group_active_members=sum(1 for x in st if x == "completed"),
+                model_prefill_inflight_groups=len(others)))
+            rows[r["assignment_id"]] = ("prefill", r)
+        q = [dict(r) for r in c.execute(
+            """SELECT q.*, j.prompt_tokens, j.max_tokens, j.temperature, j.top_p, j.model_id, j.runtime_mode,
+               j.submitter_device_id, j.created_at AS job_created, g.member_device_ids FROM inference_decode_queue q
+               JOIN inference_jobs j ON j.job_id=q.job_id JOIN inference_serving_groups g ON g.session_id=q.session_id
+               AND g.phase='decode' WHERE q.status IN ('ready','leased','active','blocked_on_transfer',
+               'blocked_on_prefill') AND j.status IN ('pending','running')""").fetchall()]
+        cohorts: Dict[tuple, dict] = {}
+        for r in q:
+            key = tuple(sorted(loads(r["member_device_ids"], [])))
+            st = cohorts.setdefault(key, dict(ready=0, blocked=0, blocked_prefill=0, leased=0, active=0, oldest=None))
+            if r["status"] == "ready":
+                st["ready"] += 1
+                t = iso(r["updated_at"])
+                st["oldest"] = t if st["oldest"] is None else min(st["oldest"], t)
+            elif r["status"] == "blocked_on_transfer":
+                st["blocked"] += 1
+            elif r["status"] == "blocked_on_prefill":
+                st["blocked_prefill"] += 1
+                st["blocked"] += 1
+            elif r["status"] == "leased":
+                st["leased"] += 1
+            elif r["status"] == "active":
+                st["active"] += 1
+        for r in q:
+            key = tuple(sorted(loads(r["member_device_ids"], [])))
+            if device_id not in key or r["status"] == "blocked_on_prefill":
+                continue
+            st = cohorts[key]
+            own = r["lease_device_id"] == device_id
+            if r["status"] == "ready":
+                gs = "decode_ready"
+            elif own:
+                gs = "decode_active"
+            else:
+                gs = "decode_member"
+            cands.append(sched.Candidate(
+                assignment_id="decode:" + r["session_id"], job_id=r["job_id"], session_id=r["session_id"],
+                phase="decode", group_status=gs, model_id=r["model_id"],
+                runtime_mode=r["runtime_mode"] or "throughput_first", submitted_by_device_id=r["submitter_device_id"] or "",
+                created_at=iso(r["job_created"]), decode_queue_status=r["status"], decode_ready_at=iso(r["updated_at"]),
+                decode_lease_owner_device_id=r["lease_device_id"], decode_lease_expires_at=(
+                    iso(r["lease_expires"]) if r["lease_expires"] else None),
+                decode_updated_at=iso(r["updated_at"]), decode_cohort_ready_sessions=st["ready"],
+                decode_cohort_blocked_sessions=st["blocked"], decode_cohort_blocked_prefill_sessions=st["blocked_prefill"],
+                decode_cohort_oldest_ready_at=st["oldest"], decode_cohort_leased_sessions=st["leased"],
+                decode_cohort_active_sessions=st["active"]))
+            rows["decode:" + r["session_id"]] = ("decode", r, key)
+        snap = sched.Snapshot()
+        for r in c.execute("SELECT submitter_device_id, model_id, COUNT(*) AS n FROM inference_jobs WHERE status="
+                           "'running' GROUP BY submitter_device_id, model_id").fetchall():
+            snap.active_jobs_by_submitter[r["submitter_device_id"] or ""] = \
+                snap.active_jobs_by_submitter.get(r["submitter_device_id"] or "", 0) + r["n"]
+            snap.active_jobs_by_model[r["model_id"]] = snap.active_jobs_by_model.get(r["model_id"], 0) + r["n"]
+        online = c.execute("SELECT COUNT(*), COALESCE(SUM(CASE tier WHEN 'tier0' THEN 1 WHEN 'tier1' THEN 2 "
+                           "WHEN 'tier3' THEN 8 WHEN 'tier4' THEN 16 ELSE 4 END), 0) FROM devices WHERE "
+                           "status='online'").fetchone()
+        snap.online_worker_count = max(1, online[0])
+        snap.online_capacity_units = max(1, online[1])
+        return cands, rows, snap
+
+    def claim(self, device_id: str, max_decode_sessions: int = 64, mode: str = "fit_first") -> dict:
+        """Claim-time scheduling (``scheduler.select_claim``): an in-flight prefill group first, then a
+        prefill whose decode cohort waits, then the best-ranked runnable work; a decode claim
+        leases the cohort of runnable sessions sharing the chosen session's decode group (one lease)."""
         self.reconcile_stale_leases()
         dev = self.db.one("SELECT * FROM devices WHERE device_id=?", (device_id,))
         if dev is None:
             raise NotFound(f"device {device_id} not registered")
         with self.db.tx() as c:
-            row = c.execute("""SELECT a.*, j.prompt_tokens, j.max_tokens, j.temperature, j.top_p, j.model_id,
-                               j.network_id, j.runtime_mode FROM inference_job_assignments a
-                               JOIN inference_jobs j ON j.job_id=a.job_id
-                               WHERE a.device_id=? AND a.phase='prefill' AND a.status='pending'
-                               AND j.status IN ('pending','running') ORDER BY a.created_at LIMIT 1""",
-                            (device_id,)).fetchone()
-            if row is not None:
-                row = dict(row)
+            cands, rows, snap = self._claim_candidates(c, device_id)
+            decision = sched.select_claim(cands, device_id, self._iso(_now()), mode, snap=snap)
+            if decision.blocked:
+                reasons: Dict[str, int] = {}
+                for b in decision.blocked:
+                    reasons[b.reason] = reasons.get(b.reason, 0) + 1
+                c.execute("INSERT INTO inference_scheduler_events (network_id, job_id, event, details, created_at) "
+                          "VALUES (?,?,?,?,?)", (dev["network_id"], None, "claim_blocked",
+                                                 dumps({"device_id": device_id, "reasons": reasons}), _now()))
+            sel = decision.selected_assignment_id
+            if sel is None:
+                return {"kind": "idle", "assignments": [],
+                        "blocked": [{"session_id": b.session_id, "reason": b.reason} for b in decision.blocked]}
+            if rows[sel][0] == "prefill":
+                row = rows[sel][1]
                 lease_id, exp = self._lease()
                 c.execute("UPDATE inference_job_assignments SET status='leased', lease_id=?, lease_expires=?, "
                           "updated_at=? WHERE assignment_id=?", (lease_id, exp, _now(), row["assignment_id"]))
@@ -377,32 +518,35 @@ class ControlPlane:
                           (_now(), row["session_id"]))
                 return {"kind": "prefill", "lease_id": lease_id, "lease_expires": exp,
                         "assignments": [self._assignment_view(row)]}
-            ready = [dict(r) for r in c.execute(
-                """SELECT q.*, j.prompt_tokens, j.max_tokens, j.temperature, j.top_p, j.model_id, j.runtime_mode,
-                   g.member_device_ids FROM inference_decode_queue q JOIN inference_jobs j ON j.job_id=q.job_id
-                   JOIN inference_serving_groups g ON g.session_id=q.session_id AND g.phase='decode'
-                   WHERE q.status='ready' ORDER BY q.decode_steps_served, q.fairness_epoch LIMIT ?""",
-                (max_decode_sessions * 4,)).fetchall()]
-            cohort = [r for r in ready if device_id in loads(r["member_device_ids"], [])][:max_decode_sessions]
-            if not cohort:
-                return {"kind": "idle", "assignments": []}
+            key = rows[sel][2]
+            now_iso = self._iso(_now())
+            cohort = [cd for cd in cands if cd.phase == "decode" and rows[cd.assignment_id][2] == key and
+                      not isinstance(sched.classify(cd, device_id, now_iso), tuple)]
+            cohort.sort(key=lambda cd: (sched.decode_session_order_time(sched.Runnable(cd, cd.decode_ready_at or "")),
+                                        cd.assignment_id))
+            cohort = cohort[:max_decode_sessions]
             lease_id, exp = self._lease()
             out = []
-            for r in cohort:
-                c.execute("UPDATE inference_decode_queue SET status='leased', lease_id=?, lease_device_id=?, "
-                          "lease_expires=?, updated_at=? WHERE session_id=?",
-                          (lease_id, device_id, exp, _now(), r["session_id"]))
-                c.execute("UPDATE inference_sessions SET status='decoding', phase='decode', updated_at=? "
-                          "WHERE session_id=?", (_now(), r["session_id"]))
+            for cd in cohort:
+                r = rows[cd.assignment_id][1]
+                attached = cd.decode_queue_status in ("leased", "active")
+                if not attached:
+                    c.execute("UPDATE inference_decode_queue SET status='leased', lease_id=?, lease_device_id=?, "
+                              "lease_expires=?, updated_at=? WHERE session_id=?",
+                              (lease_id, device_id, exp, _now(), r["session_id"]))
+                    c.execute("UPDATE inference_sessions SET status='decoding', phase='decode', updated_at=? "
+                              "WHERE session_id=?", (_now(), r["session_id"]))
                 ckpt = c.execute("SELECT payload FROM inference_session_checkpoints WHERE session_id=?",
                                  (r["session_id"],)).fetchone()
                 out.append({"job_id": r["job_id"], "session_id": r["session_id"], "phase": "decode",
                             "prompt_tokens": loads(r["prompt_tokens"]), "max_tokens": r["max_tokens"],
                             "temperature": r["temperature"], "top_p": r["top_p"], "model_id": r["model_id"],
-                            "runtime_mode": r["runtime_mode"], "has_checkpoint": ckpt is not None})
+                            "runtime_mode": r["runtime_mode"], "has_checkpoint": ckpt is not None,
+                            "attached_to_lease": r["lease_id"] if attached else None})
             c.execute("INSERT INTO inference_decode_batch_events (network_id, device_id, batch_size, kv_tokens, "
-                      "created_at) VALUES (?,?,?,?,?)", (cohort[0]["network_id"], device_id, len(out),
-                                                         sum(r["kv_seq_len"] for r in cohort), _now()))
+                      "created_at) VALUES (?,?,?,?,?)", (rows[cohort[0].assignment_id][1]["network_id"], device_id,
+                                                         len(out), sum(rows[cd.assignment_id][1]["kv_seq_len"]
+                                                                       for cd in cohort), _now()))
             return {"kind": "decode", "lease_id": lease_id, "lease_expires": exp, "assignments": out}
 
     @staticmethod
@@ -464,7 +608,10 @@ class ControlPlane:
                 pending = c.execute("SELECT COUNT(*) FROM inference_job_assignments WHERE job_id=? AND phase='prefill' "
                                     "AND status!='completed'", (job_id,)).fetchone()[0]
                 if pending == 0:
-                    status = "blocked_on_transfer" if kv_transfer else "ready"
+                    handoff = loads(job["plan"], {}).get("kv_transfer_policy") == "checkpoint_handoff"
+                    has_ckpt = c.execute("SELECT 1 FROM inference_session_checkpoints WHERE job_id=?",
+                                         (job_id,)).fetchone() is not None
+                    status = "blocked_on_transfer" if (kv_transfer or (handoff and not has_ckpt)) else "ready"
                     c.execute("UPDATE inference_decode_queue SET status=?, kv_seq_len=?, fairness_epoch="
                               "(SELECT COALESCE(MAX(fairness_epoch),0)+1 FROM inference_decode_queue), updated_at=? "
                               "WHERE job_id=?", (status, kv_cache_seq_len, _now(), job_id))
@@ -564,11 +711,17 @@ class ControlPlane:
         return {"entries": rows, "counts": counts}
 
     # ------------------------------------------------------------------------------------ checkpoints, KV
-    def upload_session_checkpoint(self, job_id: str, session_id: str, payload: bytes, token_index: int = 0) -> dict:
+    def upload_session_checkpoint(self, job_id: str, session_id: str, payload: bytes, token_index: int = 0,
+                                  source_device_id: Optional[str] = None) -> dict:
         with self.db.tx() as c:
-            c.execute("INSERT INTO inference_session_checkpoints VALUES (?,?,?,?,?) ON CONFLICT(job_id, session_id) "
+            c.execute("INSERT INTO inference_session_checkpoints VALUES (?,?,?,?,?,?) ON CONFLICT(job_id, session_id) "
                       "DO UPDATE SET payload=excluded.payload, token_index=excluded.token_index, "
-                      "created_at=excluded.created_at", (job_id, session_id, payload, token_index, _now()))
+                      "created_at=excluded.created_at, source_device_id=excluded.source_device_id",
+                      (job_id, session_id, payload, token_index, _now(), source_device_id))
+            # a checkpoint-handoff decode group waiting for the prefill's KV can start now
+            c.execute("UPDATE inference_decode_queue SET status='ready', updated_at=? WHERE session_id=? AND "
+                      "status='blocked_on_transfer' AND NOT EXISTS (SELECT 1 FROM inference_session_kv_transfers t "
+                      "WHERE t.session_id=? AND t.status='pending')", (_now(), session_id, session_id))
         return {"job_id": job_id, "session_id": session_id, "bytes": len(payload),
                 "sha256": hashlib.sha256(payload).hexdigest()}
 
@@ -612,7 +765,8 @@ class ControlPlane:
 
     # ------------------------------------------------------------------------------------ failover / presence
     def evaluate_failover(self, lost_device_ids: List[str]) -> List[dict]:
-        """Regroup every job touched by the lost devices; returns the decisions taken."""
+        """Regroup every running job touched by the lost devices (``failover.FailoverEngine``);
+        returns the decisions taken."""
         lost = set(lost_device_ids)
         decisions = []
         jobs = self.db.query("SELECT * FROM inference_jobs WHERE status IN ('pending','running')")
@@ -625,66 +779,109 @@ class ControlPlane:
             q = self.db.one("SELECT * FROM inference_decode_queue WHERE job_id=?", (job["job_id"],))
             phase = "prefill" if q is None or q["status"] == "blocked_on_prefill" else "decode"
             with self.db.tx() as c:
-                if phase == "prefill":
-                    self._fail_job(c, job, f"prefill group lost devices {sorted(parts & lost)}")
-                    d = {"job_id": job["job_id"], "strategy": "fail", "recovery_state": "failed",
-                         "resume_mode": "none", "lost_device_ids": sorted(parts & lost)}
-                else:
-                    d = self._decode_failover(c, job, plan, groups["decode"], lost, q)
+                d = self._failover_decision(c, job, plan, groups, phase, lost, q)
                 c.execute("INSERT INTO inference_regroup_events (job_id, session_id, decision, details, created_at) "
                           "VALUES (?,?,?,?,?)", (job["job_id"], q["session_id"] if q else None, d["strategy"],
                                                  dumps(d), _now()))
             decisions.append(d)
         return decisions
 
-    def _decode_failover(self, c, job, plan, group, lost, q) -> dict:
-        members = group["members"]
-        survivors = [m for m in members if m["device_id"] not in lost]
-        lost_ids = sorted(m["device_id"] for m in members if m["device_id"] in lost)
-        has_ckpt = c.execute("SELECT 1 FROM inference_session_checkpoints WHERE session_id=?",
-                             (q["session_id"],)).fetchone() is not None
-        resume = "requires_checkpoint_transfer" if has_ckpt else "none"
-        # replacement candidates: online ring members of the network not already serving this group
-        ring = [dict(r) for r in c.execute(
-            "SELECT m.device_id, m.column_start, m.column_end FROM ring_members m JOIN devices d ON "
-            "d.device_id=m.device_id WHERE m.network_id=? AND d.status='online'", (job["network_id"],)).fetchall()]
-        in_group = {m["device_id"] for m in members}
-        spare = [r for r in ring if r["device_id"] not in in_group and r["device_id"] not in lost]
-        strategy, new_members = "fail", None
-        if spare and len(spare) >= len(lost_ids) and has_ckpt:
-            repl = spare[:len(lost_ids)]
-            new_members = survivors + [{**m, "device_id": r["device_id"]} for m, r in
-                                       zip([m for m in members if m["device_id"] in lost], repl)]
-            strategy = "replace"
-        elif survivors and has_ckpt:
-            covered = sorted((m["shard_column_start"], m["shard_column_end"]) for m in survivors)
-            full = covered and covered[0][0] == 0 and all(covered[i][1] == covered[i + 1][0]
-                                                          for i in range(len(covered) - 1))
-            cfg, _ = self.model_config(job["model_id"])
-            if full and covered[-1][1] == cfg.hidden_dim:
-                new_members = survivors
-                strategy = "shrink"
-            elif len(survivors) >= 1:
-                # survivors re-shard the full model (FullReplica-capable workers)
-                new_members = [{**m, "shard_column_start": 0, "shard_column_end": cfg.hidden_dim,
-                                "worker_position": i, "total_workers": 1} for i, m in enumerate(survivors[:1])]
-                strategy = "shrink"
-        if strategy == "fail":
-            self._fail_job(c, job, f"decode group lost devices {lost_ids} without a recoverable regroup")
-            return {"job_id": job["job_id"], "strategy": "fail", "recovery_state": "failed", "resume_mode": "none",
-                    "lost_device_ids": lost_ids}
+    @staticmethod
+    def _plan_members(group: dict) -> List[Member]:
+        return [Member(m["device_id"], m.get("worker_position", i), m["shard_column_start"], m["shard_column_end"],
+                       contributed_memory=m.get("contributed_memory", 0),
+                       assigned_capacity_units=m.get("assigned_capacity_units", 4),
+                       listen_addrs=["dataplane://" + m["device_id"]])
+                for i, m in enumerate(group["members"])]
+
+    def _failover_decision(self, c, job, plan, groups, phase, lost, q) -> dict:
+        group = groups["prefill" if phase == "prefill" else "decode"]
+        members = self._plan_members(group)
+        sess = self.db.one("SELECT * FROM inference_sessions WHERE job_id=?", (job["job_id"],)) or {}
+        ck = c.execute("SELECT source_device_id, created_at FROM inference_session_checkpoints WHERE job_id=? "
+                       "ORDER BY created_at DESC LIMIT 1", (job["job_id"],)).fetchone()
+        ck_dev = None
+        if ck is not None:
+            src = ck["source_device_id"] or sess.get("kv_owner_device_id")
+            st = c.execute("SELECT status FROM devices WHERE device_id=?", (src,)).fetchone()
+            # the control plane stores the checkpoint payload itself, so it survives its source device
+            ck_dev = src if (st is not None and st["status"] == "online" and src not in lost) else "control-plane"
+        session = fo.SessionView(
+            session_id=sess.get("session_id", ""), status="decode_active" if (q and q["status"] in ("leased", "active"))
+            else "decode_ready", phase=phase, participants=[m.device_id for m in members],
+            kv_owner_device_id=sess.get("kv_owner_device_id") or members[0].device_id,
+            kv_sequence_position=int(sess.get("kv_seq_len") or 0), latest_checkpoint_device_id=ck_dev,
+            latest_checkpoint_created_at=self._iso(ck["created_at"]) if ck is not None else None,
+            segment_id=f"segment-{sess.get('session_id', '')}-{phase}")
+        refreshed = None
+        if phase == "decode":
+            live = self._members(job["network_id"], job["model_id"], exclude=lost)
+            try:
+                cur = planner_mod.Plan(plan.get("plan_id", ""), plan.get("runtime_mode", "latency_first"), [],
+                                       [m for m in members if m.device_id not in lost] or members, "", "")
+                re = planner_mod.refresh_decode_plan(self.manifest(job["model_id"]), cur, live)
+                if all(m.device_id not in lost for m in re.decode):
+                    refreshed = ([m.device_id for m in re.decode], planner_mod.select_kv_owner(re.decode))
+                    known = {m.device_id for m in members}
+                    members = members + [m for m in re.decode if m.device_id not in known]
+            except (planner_mod.PlanningError, LayoutError):
+                refreshed = None
+        transfers = [fo.KvTransfer(f"segment-{t['session_id']}-decode", t["source_device_id"], t["target_device_id"],
+                                   "live_kv_handoff", t["status"], int(sess.get("kv_seq_len") or 0))
+                     for t in c.execute("SELECT * FROM inference_session_kv_transfers WHERE job_id=?",
+                                        (job["job_id"],)).fetchall()]
+        support = fo.SupportGroups(kv={m.device_id for m in members}, recovery={m.device_id for m in members})
+        d = fo.FailoverEngine().evaluate(session, members, sorted(lost), q["status"] if q else None, transfers,
+                                         refreshed, support if plan.get("live_kv_handoff") else None)
+        out = d.to_json()
+        out["job_id"] = job["job_id"]
+        out["participant_device_ids"] = d.target_participant_device_ids
+        if d.recovery_state == "failed":
+            self._fail_job(c, job, d.reason)
+            return out
+        if d.recovery_state == "healthy":
+            return out
+        by_id = {m.device_id: m for m in members}
+        new_members = []
+        for i, dev_id in enumerate(d.target_participant_device_ids):
+            m = by_id[dev_id]
+            new_members.append({**m.to_json(), "worker_position": i,
+                                "total_workers": len(d.target_participant_device_ids)})
         group = dict(group)
         group["members"] = new_members
         plan = dict(plan)
         plan["execution_groups"] = [g if g["phase"] != "decode" else group for g in plan["execution_groups"]]
         c.execute("UPDATE inference_jobs SET plan=?, updated_at=? WHERE job_id=?", (dumps(plan), _now(), job["job_id"]))
         c.execute("UPDATE inference_serving_groups SET member_device_ids=? WHERE group_id=?",
-                  (dumps([m["device_id"] for m in new_members]), group["group_id"]))
-        c.execute("UPDATE inference_decode_queue SET status='ready', lease_id=NULL, lease_device_id=NULL, "
-                  "lease_expires=NULL, updated_at=? WHERE session_id=?", (_now(), q["session_id"]))
-        return {"job_id": job["job_id"], "strategy": strategy, "recovery_state": "resume_ready",
-                "resume_mode": resume, "lost_device_ids": lost_ids,
-                "participant_device_ids": [m["device_id"] for m in new_members]}
+                  (dumps(d.target_participant_device_ids), group["group_id"]))
+        c.execute("UPDATE inference_sessions SET kv_owner_device_id=?, updated_at=? WHERE job_id=?",
+                  (d.next_kv_owner_device_id, _now(), job["job_id"]))
+        c.execute("UPDATE inference_decode_queue SET status=?, lease_id=NULL, lease_device_id=NULL, lease_expires=NULL, "
+                  "updated_at=? WHERE session_id=?", (d.decode_queue_status, _now(), q["session_id"]))
+        if d.resume_mode in ("requires_live_kv_transfer", "requires_checkpoint_transfer"):
+            for dev_id in d.replacement_device_ids or d.target_participant_device_ids:
+                c.execute("INSERT INTO inference_session_kv_transfers VALUES (?,?,?,?,?,'pending',?,?)",
+                          (_uid(), job["job_id"], q["session_id"], d.transfer_source_device_id, dev_id, _now(), _now()))
+        return out
+
+    def cleanup_terminal_state(self) -> dict:
+        """Release what finished or failed sessions still hold: decode-queue leases of terminal jobs,
+        assignments leased to devices that are gone, pending KV transfers of terminal jobs
+        (``failover.rs:2158-2312``)."""
+        now = _now()
+        with self.db.tx() as c:
+            q = c.execute("UPDATE inference_decode_queue SET lease_id=NULL, lease_device_id=NULL, lease_expires=NULL, "
+                          "status=CASE WHEN status IN ('completed','failed') THEN status ELSE 'failed' END, updated_at=? "
+                          "WHERE job_id IN (SELECT job_id FROM inference_jobs WHERE status IN "
+                          "('completed','failed','cancelled')) AND (lease_id IS NOT NULL OR status NOT IN "
+                          "('completed','failed'))", (now,)).rowcount
+            a = c.execute("UPDATE inference_job_assignments SET status='pending', lease_id=NULL, lease_expires=NULL, "
+                          "updated_at=? WHERE status IN ('leased','acked') AND device_id NOT IN (SELECT device_id FROM "
+                          "devices WHERE status='online')", (now,)).rowcount
+            t = c.execute("UPDATE inference_session_kv_transfers SET status='cancelled', updated_at=? WHERE "
+                          "status='pending' AND job_id IN (SELECT job_id FROM inference_jobs WHERE status IN "
+                          "('completed','failed','cancelled'))", (now,)).rowcount
+        return {"queue_leases_released": q, "orphaned_assignments": a, "transfers_cancelled": t}
 
     def presence_sweep(self, now: Optional[float] = None) -> List[str]:
         """Mark devices silent for longer than the stale timeout as stale and regroup their work."""
@@ -695,6 +892,7 @@ class ControlPlane:
             with self.db.tx() as c:
                 c.executemany("UPDATE devices SET status='stale' WHERE device_id=?", [(d,) for d in stale])
             self.evaluate_failover(stale)
+            self.cleanup_terminal_state()
         return stale
 
     # ------------------------------------------------------------------------------------ status

@@ -137,17 +137,108 @@ def test_failover_prefill_loss_fails_and_decode_loss_regroups():
         cp.claim(d)
         cp.claim(d)
         cp.report_progress(j2["job_id"], d, "prefill", 1, kv_cache_seq_len=2)
-    cp.upload_session_checkpoint(j2["job_id"], j2["session_id"], b"ckpt")
-    cp.join_ring("c", net, "tiny")  # spare member for replacement
+    cp.upload_session_checkpoint(j2["job_id"], j2["session_id"], b"ckpt", source_device_id="a")
+    cp.join_ring("c", net, "tiny")
+    # c serves a full replica of the model (as after a shard handoff): it can replace b
+    with cp.db.tx() as c:
+        c.execute("UPDATE ring_members SET column_start=0, column_end=512 WHERE device_id='c'")
     decisions = {d["job_id"]: d for d in cp.evaluate_failover(["b"])}
     assert decisions[j1["job_id"]]["strategy"] == "fail"
     assert cp.job_status(j1["job_id"])["status"] == "failed"
     d2 = decisions[j2["job_id"]]
-    assert d2["strategy"] in ("replace", "shrink") and d2["resume_mode"] == "requires_checkpoint_transfer"
-    assert "b" not in d2["participant_device_ids"]
+    assert d2["strategy"] == "replace" and d2["resume_mode"] == "requires_checkpoint_transfer"
+    assert d2["recovery_state"] == "paused" and d2["participant_device_ids"] == ["c"]
+    assert d2["transfer_source_device_id"] == "a"
+    st = cp.job_status(j2["job_id"])
+    assert st["decode_queue"]["status"] == "blocked_on_transfer"
+    assert [m["device_id"] for m in st["plan"]["execution_groups"][1]["members"]] == ["c"]
+    # the replacement is not claimable until the KV arrives; the transfer completes -> ready
+    assert cp.claim("c")["kind"] == "idle"
+    t = cp.pending_kv_transfers("c")
+    assert len(t) == 1 and t[0]["source_device_id"] == "a"
+    cp.report_kv_transfer(j2["job_id"], j2["session_id"], "a", "c", status="completed",
+                          transfer_id=t[0]["transfer_id"])
     assert cp.job_status(j2["job_id"])["decode_queue"]["status"] == "ready"
+    w = cp.claim("c")
+    assert w["kind"] == "decode" and w["assignments"][0]["session_id"] == j2["session_id"]
     ev = cp.ledger_summary(net)
     assert ev["events"] > 0
+
+
+def test_failover_shrinks_to_a_surviving_full_replica_and_cleans_up():
+    cp = _cp()
+    net = cp.create_network("n")["network_id"]
+    for d in ("a", "b"):
+        cp.register_device(d, net)
+    cp.join_ring("a", net, "tiny")
+    cp.join_ring("b", net, "tiny")
+    j = cp.submit_inference(net, "tiny", prompt_tokens=[5, 6], max_tokens=4, submitter_device_id="a")
+    for d in ("a", "b"):
+        cp.claim(d)
+        cp.report_progress(j["job_id"], d, "prefill", 1, kv_cache_seq_len=2)
+    assert cp.claim("a")["kind"] == "decode"
+    # b is lost while a, which also holds every column of the decode group, keeps serving
+    with cp.db.tx() as c:
+        c.execute("UPDATE ring_members SET column_start=0, column_end=512 WHERE device_id='a'")
+    plan = cp.job_status(j["job_id"])["plan"]
+    for m in plan["execution_groups"][1]["members"]:
+        m["shard_column_start"], m["shard_column_end"] = 0, 512
+    with cp.db.tx() as c:
+        c.execute("UPDATE inference_jobs SET plan=? WHERE job_id=?", (__import__("json").dumps(plan), j["job_id"]))
+    d = cp.evaluate_failover(["b"])[0]
+    assert d["strategy"] == "shrink" and d["resume_mode"] == "immediate" and d["participant_device_ids"] == ["a"]
+    assert cp.job_status(j["job_id"])["decode_queue"]["status"] == "ready"
+    # a finished job keeps no leases after cleanup
+    cp.cancel_job(j["job_id"])
+    with cp.db.tx() as c:
+        c.execute("UPDATE inference_decode_queue SET lease_id='stale' WHERE job_id=?", (j["job_id"],))
+    out = cp.cleanup_terminal_state()
+    assert out["queue_leases_released"] == 1
+    assert cp.job_status(j["job_id"])["decode_queue"]["lease_id"] is None
+
+
+def test_claim_reports_blocked_reasons_and_respects_group_leader():
+    cp = _cp()
+    net = cp.create_network("n")["network_id"]
+    for d in ("a", "b"):
+        cp.register_device(d, net)
+    cp.join_ring("a", net, "tiny")
+    cp.join_ring("b", net, "tiny")
+    cp.submit_inference(net, "tiny", prompt_tokens=[1, 2], max_tokens=4)
+    # the follower cannot open the prefill group; the leader can, then the follower joins it
+    w = cp.claim("b")
+    assert w["kind"] == "idle" and w["blocked"][0]["reason"] == "lease_held_by_peer"
+    assert cp.claim("a")["kind"] == "prefill"
+    assert cp.claim("b")["kind"] == "prefill"
+    ev = cp.db.query("SELECT * FROM inference_scheduler_events WHERE event='claim_blocked'")
+    assert ev and "lease_held_by_peer" in ev[0]["details"]
+
+
+def test_disaggregated_plan_blocks_decode_until_checkpoint_arrives():
+    cp = _cp()
+    net = cp.create_network("n")["network_id"]
+    for d, tier in (("a", "tier2"), ("b", "tier2"), ("c", "tier3")):
+        cp.register_device(d, net, tier=tier)
+    for d in ("a", "b", "c"):
+        cp.join_ring(d, net, "tiny")
+    # a and b tile the columns (the prefill TP group); c, a larger worker, holds a full replica and
+    # scores best for decode, so the plan hands the KV from the prefill group to c by checkpoint
+    with cp.db.tx() as c:
+        c.execute("UPDATE ring_members SET column_start=0, column_end=256 WHERE device_id='a'")
+        c.execute("UPDATE ring_members SET column_start=256, column_end=512 WHERE device_id='b'")
+        c.execute("UPDATE ring_members SET column_start=0, column_end=512 WHERE device_id='c'")
+    j = cp.submit_inference(net, "tiny", prompt_tokens=[1, 2, 3], max_tokens=3)
+    plan = j["plan"]
+    assert plan["kv_transfer_policy"] == "checkpoint_handoff"
+    assert [m["device_id"] for m in plan["execution_groups"][0]["members"]] == ["a", "b"]
+    assert [m["device_id"] for m in plan["execution_groups"][1]["members"]] == ["c"]
+    for d in ("a", "b"):
+        assert cp.claim(d)["kind"] == "prefill"
+        cp.report_progress(j["job_id"], d, "prefill", 1, kv_cache_seq_len=3)
+    assert cp.job_status(j["job_id"])["decode_queue"]["status"] == "blocked_on_transfer"
+    cp.upload_session_checkpoint(j["job_id"], j["session_id"], b"kv", source_device_id="a")
+    assert cp.job_status(j["job_id"])["decode_queue"]["status"] == "ready"
+    assert cp.claim("c")["kind"] == "decode"
 
 
 def test_presence_marks_stale_and_reconciles_leases():
