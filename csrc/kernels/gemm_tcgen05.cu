@@ -62,8 +62,8 @@ struct ArTail {
   int rank, world, T, H, t_max;
   unsigned long long ws[AR_TAIL_MAX_RANKS];  // symmetric workspace base of every rank (as mapped here)
   unsigned long long mc;                     // multicast base of the workspace (0: plain peer stores)
-  long off_flags;    // uint32 [2 phases][AR_TAIL_MAX_RANKS sources], in every rank's workspace
-  long off_counts;   // uint32 [2] arrival counters of this rank's CTAs (zero between launches)
+  long off_flags;    // uint32 [2 phases][AR_TAIL_MAX_RANKS sources][AR_TAIL_MAX_CTAS], in every rank's workspace
+  long off_counts;   // unused (kept so the configuration table keeps its layout)
   long off_push;     // bf16 [world sources][t_max][H] pushed partial rows (this call's parity)
   long off_resid;    // bf16 [t_max][H] residual; a rank keeps its owned rows current
   long off_normed;   // bf16 [t_max][H] normed rows, complete on every rank after the launch
@@ -979,116 +979,128 @@ __device__ __forceinline__ void ck_epilogue(const GemmParams& p, const Smem& s, 
 // ----------------------------------------------------------------------------------------------
 // Fused all-reduce tail (swap-AB bf16 GEMM with push mode 1; epilogue warps, 128 threads).
 //
-// Protocol of one launch, epoch e = local epoch word + 1:
-//  phase 0  every CTA has pushed its partial rows (each storing thread fenced at system scope);
-//           the last of this rank's CTAs to arrive (gpu-scope arrival counter) raises flag[0][rank]
-//           = e in every rank's workspace;
-//  reduce   CTA i < min(owned rows, grid) waits (bounded) for flag[0][*] >= e from every rank,
-//           sums its owned rows over the ranks' pushed slots (fp32, source order), adds the
-//           residual (stored back rounded to bf16, locally), applies RMSNorm to the rounded value
-//           and stores the normed row into every rank;
-//  phase 1  the last reducing CTA raises flag[1][rank] = e everywhere (a rank that owns no rows
-//           raises it from CTA 0 at once);
-//  exit     CTA 0 waits (bounded) for flag[1][*] >= e from every rank, then stores e as the new
-//           epoch. The next kernel's griddepcontrol.wait therefore sees every normed row.
-// Flags only grow, so nothing is reset between launches; the arrival counters are reset by the
-// CTA that completes them. A slot is rewritten only by the next launch, which cannot start its
-// pushes before every rank left this one (phase 1), so one set of push slots would do; the caller
-// still alternates two. Every wait records ERR_PEER_TIMEOUT and gives up after `timeout_ns`.
+// Protocol of one launch, epoch e = local epoch word + 1. Flags live in every rank's workspace as
+// flag[phase][source rank][source CTA] and only grow, so nothing is reset between launches.
+//  phase 0  after the CTA barrier that follows its pushes, one thread of every CTA issues one
+//           system-scope fence (cumulative over the barrier: it orders every thread's pushes of
+//           the CTA) and stores flag[0][rank][cta] = e into every rank;
+//  reduce   CTA i < min(owned rows, grid) waits (bounded) until every rank's every CTA raised its
+//           phase-0 flag here, sums its owned rows over the ranks' pushed slots (fp32, source
+//           order), adds the residual (stored back rounded to bf16, locally), applies RMSNorm to
+//           the rounded value and stores the normed row into every rank;
+//  phase 1  the same fence + flag store pattern for flag[1][rank][reducing cta];
+//  exit     CTA 0 waits (bounded) for phase 1 of every reducing CTA of every rank (their number
+//           follows from T and the row split), then stores e as the new epoch. The next kernel's
+//           griddepcontrol.wait therefore sees every normed row.
+// A push slot is rewritten only by the next launch, which cannot start its pushes before every rank
+// left this one (phase 1), so one set of slots would do; the caller still alternates two. Every
+// wait records ERR_PEER_TIMEOUT and gives up after `timeout_ns`.
 // ----------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t* ar_flag(const ArTail& a, int dst, int phase, int src) {
-  return reinterpret_cast<uint32_t*>(a.ws[dst] + a.off_flags) + phase * AR_TAIL_MAX_RANKS + src;
+constexpr int AR_TAIL_MAX_CTAS = 256;
+
+__device__ __forceinline__ uint32_t* ar_flag(const ArTail& a, int dst, int phase, int src, int cta) {
+  return reinterpret_cast<uint32_t*>(a.ws[dst] + a.off_flags) +
+         ((long)(phase * AR_TAIL_MAX_RANKS + src) * AR_TAIL_MAX_CTAS + cta);
 }
 
-// Arrival of this CTA at `phase`; the CTA completing `expected` arrivals signals every rank.
-__device__ __forceinline__ void ar_arrive(const ArTail& a, int phase, uint32_t e, uint32_t expected, int et) {
-  named_bar_sync(1, 128);  // every thread of the CTA fenced its stores before this barrier
+// Called by all 128 epilogue threads right after a barrier that follows their stores.
+__device__ __forceinline__ void ar_signal(const ArTail& a, int phase, uint32_t e, int et) {
   if (et == 0) {
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(a.ws[a.rank] + a.off_counts) + phase;
     fence_acq_rel_sys();
-    const uint32_t old = atom_add_acq_rel_gpu(cnt, 1u);
-    if (old + 1u == expected) {
-      st_relaxed_gpu(cnt, 0u);
-      fence_acq_rel_sys();
-      for (int d = 0; d < a.world; ++d) st_release_sys(ar_flag(a, d, phase, a.rank), e);
-    }
+    for (int d = 0; d < a.world; ++d) st_relaxed_sys(ar_flag(a, d, phase, a.rank, blockIdx.x), e);
   }
 }
 
-// Bounded wait for flag[phase][src] >= e from every rank; uniform result across the 128 threads.
-__device__ __forceinline__ bool ar_wait(const GemmParams& p, int phase, uint32_t e, int et, volatile int* s_ok) {
+// rows rank r owns when T rows are split into near-equal ranges (larger ranges first)
+__device__ __forceinline__ int ar_rows_of(const ArTail& a, int r) {
+  return a.T / a.world + (r < a.T % a.world ? 1 : 0);
+}
+
+// Bounded wait until flag[phase][src][c] >= e here for every src and every c < ncta(src) (all 128
+// threads poll in parallel); uniform result across the 128 threads.
+template <typename NCta>
+__device__ __forceinline__ bool ar_wait(const GemmParams& p, int phase, uint32_t e, int et, volatile int* s_ok,
+                                        NCta ncta) {
   const ArTail& a = p.ar;
   if (et == 0) *s_ok = 1;
   named_bar_sync(1, 128);
-  if (et < a.world && !wait_flag_geq(ar_flag(a, a.rank, phase, et), e, a.timeout_ns, p.err)) *s_ok = 0;
+  bool ok = true;
+  for (int src = 0; src < a.world && ok; ++src) {
+    const int n = ncta(src);
+    for (int c = et; c < n && ok; c += 128)
+      ok = wait_flag_geq(ar_flag(a, a.rank, phase, src, c), e, a.timeout_ns, p.err);
+  }
+  if (!ok) *s_ok = 0;
   named_bar_sync(1, 128);
   return *s_ok != 0;
 }
 
-// One owned token row: H features, 8 per 16-byte chunk, chunks et + 128 j (j < MAXC), summed in
-// groups of 4 chunks (fp32 accumulators of one group live at a time; the rounded residual of every
-// chunk is kept packed for the normalisation pass).
-template <int MAXC>
+// One owned token row: H features, 8 per 16-byte chunk, chunks et + 128 j (j < MAXC), processed
+// in groups of G chunks; within a group the residual and every source's chunks are all loaded
+// before any is added (one memory round trip per group). The rounded residual of every chunk is
+// kept packed for the normalisation pass when MAXC <= 4; wider rows (H > 4096) read back the
+// residual they just stored instead, which keeps the register footprint of the tail small.
+template <int MAXC, int G, int NSRC>
 __device__ __forceinline__ void ar_tail_row(const ArTail& a, long row, int et, volatile float* red) {
+  constexpr bool KEEP = MAXC <= 4;
   const int nvec = a.H / 8;
   uint4* resid = reinterpret_cast<uint4*>(a.ws[a.rank] + a.off_resid) + row * nvec;
-  uint4 packed[MAXC];
+  const __nv_bfloat16* push0 = reinterpret_cast<const __nv_bfloat16*>(a.ws[a.rank] + a.off_push) + row * a.H;
+  uint4 packed[KEEP ? MAXC : 1];
   float ss = 0.f;
 #pragma unroll
-  for (int g0 = 0; g0 < MAXC; g0 += 4) {
-    float acc[4][8];
+  for (int g0 = 0; g0 < MAXC; g0 += G) {
+    uint4 rv[G];
+    uint4 d[NSRC][G];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < G; ++j) {
       const int c = et + 128 * (g0 + j);
-      if (c < nvec) {
-        const uint4 r = resid[c];
-        const uint32_t* ru = reinterpret_cast<const uint32_t*>(&r);
+      if (c < nvec) rv[j] = resid[c];
+    }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) unpack_bf16x2(ru[q], acc[j][2 * q], acc[j][2 * q + 1]);
+    for (int src = 0; src < NSRC; ++src) {
+      if (src < a.world) {
+        const uint4* part = reinterpret_cast<const uint4*>(push0 + (long)src * a.t_max * a.H);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const int c = et + 128 * (g0 + j);
+          if (c < nvec) d[src][j] = __ldcg(part + c);
+        }
       }
     }
-    // sources in rank order (deterministic); a source's chunks are all loaded before any is added
 #pragma unroll
-    for (int src = 0; src < AR_TAIL_MAX_RANKS; ++src) {
-      if (src >= a.world) break;
-      const uint4* part = reinterpret_cast<const uint4*>(
-          reinterpret_cast<const __nv_bfloat16*>(a.ws[a.rank] + a.off_push) + ((long)src * a.t_max + row) * a.H);
-      uint4 d[4];
+    for (int j = 0; j < G; ++j) {
+      const int c = et + 128 * (g0 + j);
+      if (c >= nvec) continue;
+      float acc[8];
+      const uint32_t* ru = reinterpret_cast<const uint32_t*>(&rv[j]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = et + 128 * (g0 + j);
-        if (c < nvec) d[j] = __ldcg(part + c);
-      }
+      for (int q = 0; q < 4; ++q) unpack_bf16x2(ru[q], acc[2 * q], acc[2 * q + 1]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = et + 128 * (g0 + j);
-        if (c < nvec) {
-          const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[j]);
+      for (int src = 0; src < NSRC; ++src) {  // rank order: deterministic
+        if (src < a.world) {
+          const uint32_t* du = reinterpret_cast<const uint32_t*>(&d[src][j]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             float x0, x1;
             unpack_bf16x2(du[q], x0, x1);
-            acc[j][2 * q] += x0;
-            acc[j][2 * q + 1] += x1;
+            acc[2 * q] += x0;
+            acc[2 * q + 1] += x1;
           }
         }
       }
-    }
-    // the residual is stored rounded to bf16 and the norm is taken of that stored value
+      // the residual is stored rounded to bf16 and the norm is taken of that stored value
+      uint4 pk;
+      uint32_t* pu = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = et + 128 * (g0 + j);
-      if (c < nvec) {
-        uint32_t* pu = reinterpret_cast<uint32_t*>(&packed[g0 + j]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          pu[q] = pack_bf16x2(acc[j][2 * q], acc[j][2 * q + 1]);
-          float r0, r1;
-          unpack_bf16x2(pu[q], r0, r1);
-          ss += r0 * r0 + r1 * r1;
-        }
-        resid[c] = packed[g0 + j];
+      for (int q = 0; q < 4; ++q) {
+        pu[q] = pack_bf16x2(acc[2 * q], acc[2 * q + 1]);
+        float r0, r1;
+        unpack_bf16x2(pu[q], r0, r1);
+        ss += r0 * r0 + r1 * r1;
       }
+      resid[c] = pk;
+      if constexpr (KEEP) packed[g0 + j] = pk;
     }
   }
 #pragma unroll
@@ -1104,7 +1116,10 @@ __device__ __forceinline__ void ar_tail_row(const ArTail& a, long row, int et, v
     if (c < nvec) {
       const uint4 g = gv[c];
       const uint32_t* gu = reinterpret_cast<const uint32_t*>(&g);
-      const uint32_t* pu = reinterpret_cast<const uint32_t*>(&packed[j]);
+      uint4 pk;
+      if constexpr (KEEP) pk = packed[j];
+      else pk = resid[c];  // written by this thread above
+      const uint32_t* pu = reinterpret_cast<const uint32_t*>(&pk);
       uint4 o;
       uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -1124,42 +1139,51 @@ __device__ __forceinline__ void ar_tail_row(const ArTail& a, long row, int et, v
   }
 }
 
+template <int MAXC>
+__device__ __forceinline__ void ar_tail_rows(const ArTail& a, long r0, int nrows, int et, volatile float* red) {
+  for (long row = r0 + blockIdx.x; row < r0 + nrows; row += gridDim.x) {
+    if (a.world <= 4)
+      ar_tail_row<MAXC, 4, 4>(a, row, et, red);
+    else
+      ar_tail_row<MAXC, 2, AR_TAIL_MAX_RANKS>(a, row, et, red);
+  }
+}
+
+// Runs after the CTA barrier that follows the epilogue (every push of this CTA is issued).
 __device__ __forceinline__ void ar_tail(const GemmParams& p, const Smem& s, int et, unsigned long long* trace) {
   const ArTail& a = p.ar;
   const bool tr = trace != nullptr && et == 0;
   if (tr) trace[16] = globaltimer_ns();
   volatile uint32_t* s_e = reinterpret_cast<volatile uint32_t*>(s.epi);  // [0] epoch, [1] ok
   volatile float* red = reinterpret_cast<volatile float*>(s.epi) + 4;  // [4] sum-of-squares partials
-  if (et == 0) s_e[0] = *a.epoch + 1u;
+  if (et == 0) {
+    const uint32_t e0 = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1u;
+    s_e[0] = e0;
+    ar_signal(a, 0, e0, et);  // the CTA barrier before the tail ordered every push of this CTA
+  }
   named_bar_sync(1, 128);
   const uint32_t e = s_e[0];
-  ar_arrive(a, 0, e, gridDim.x, et);
   if (tr) trace[17] = globaltimer_ns();
-  const int base = a.T / a.world, extra = a.T % a.world;
-  const long r0 = (long)a.rank * base + min(a.rank, extra);
-  const int nrows = base + (a.rank < extra ? 1 : 0);
-  const int nred = min(nrows, (int)gridDim.x);
+  const int grid = (int)gridDim.x;
+  const int nrows = ar_rows_of(a, a.rank);
+  const long r0 = (long)a.rank * (a.T / a.world) + min(a.rank, a.T % a.world);
+  const int nred = min(nrows, grid);
   volatile int* s_ok = reinterpret_cast<volatile int*>(s_e + 1);
   if ((int)blockIdx.x < nred) {
-    if (ar_wait(p, 0, e, et, s_ok)) {
+    if (ar_wait(p, 0, e, et, s_ok, [grid](int) { return grid; })) {
       if (tr) trace[18] = globaltimer_ns();
-      for (long row = r0 + blockIdx.x; row < r0 + nrows; row += gridDim.x) {
-        if (a.H <= 128 * 8 * 4)
-          ar_tail_row<4>(a, row, et, red);
-        else
-          ar_tail_row<8>(a, row, et, red);
-      }
+      if (a.H <= 128 * 8 * 4)
+        ar_tail_rows<4>(a, r0, nrows, et, red);
+      else
+        ar_tail_rows<8>(a, r0, nrows, et, red);
       if (tr) trace[19] = globaltimer_ns();
     }
-    __threadfence_system();  // this thread's normed stores (peer or multicast) before the signal
-    ar_arrive(a, 1, e, nred, et);
+    named_bar_sync(1, 128);  // every normed store of this CTA is issued
+    ar_signal(a, 1, e, et);
     if (tr) trace[20] = globaltimer_ns();
-  } else if (nred == 0 && blockIdx.x == 0 && et == 0) {
-    fence_acq_rel_sys();
-    for (int d = 0; d < a.world; ++d) st_release_sys(ar_flag(a, d, 1, a.rank), e);
   }
   if (blockIdx.x == 0) {
-    ar_wait(p, 1, e, et, s_ok);
+    ar_wait(p, 1, e, et, s_ok, [&a, grid](int src) { return min(ar_rows_of(a, src), grid); });
     if (tr) trace[21] = globaltimer_ns();
     if (et == 0) *a.epoch = e;
   }
@@ -1566,7 +1590,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
 
-  if (p.push_mode != 0 && warp >= 2) __threadfence_system();  // pushed tiles visible to the peers
+  // pushed tiles visible to the peers: per thread here, or once per CTA in the fused tail's signal
+  if (p.push_mode != 0 && !p.ar.on && warp >= 2) __threadfence_system();
   if (trace && threadIdx.x == 64) trace[6] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
@@ -1907,6 +1932,7 @@ static void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
     TORCH_CHECK(trans && epi == EPI_STORE_BF16 && p.push_mode == 1 && ar->world == p.world && ar->rank == p.my_rank &&
                     ar->T == N && ar->H == M,
                 "fused all-reduce tail: swap-AB bf16 GEMM pushing rows to their owners");
+    TORCH_CHECK(pl.grid <= AR_TAIL_MAX_CTAS, "fused all-reduce tail: at most 256 CTAs");
     p.ar = *ar;
     p.ar.on = 1;
   }

@@ -143,7 +143,11 @@ def gemm_allreduce_norm(w: torch.Tensor, x: torch.Tensor, part_view: torch.Tenso
     plan = _PLANS.get(key)
     if plan is None:
         plan = _PLANS[key] = ext().gemm_plan(M, N, K, EPI_STORE_BF16, True, x.device.index)
-    if plan[2] > 0:
+    if mode != 0:
+        # explicit schedule (tests): size the stream-K workspace for the worst case of this shape
+        tiles = ((M + 127) // 128) * ((N + plan[0] - 1) // plan[0])
+        s.ensure_gemm((tiles + s.num_sms) * 128 * plan[0], tiles)
+    elif plan[2] > 0:
         s.ensure_gemm(plan[1], plan[2])
     ext().gemm_allreduce_norm(w, x, part_view, push, cfg, gamma, eps, epoch, mode, s.gemm_ws, s.gemm_counters, s.err,
                               trace)

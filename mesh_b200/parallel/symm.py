@@ -3,8 +3,8 @@
 One allocation per rank, mapped into every peer of the TP group (CUDA VMM/IPC through
 ``torch.distributed._symmetric_memory``). Layout (byte offsets, identical on every rank):
 
-    [flags: 2 phases x 256 blocks x 8 ranks x u32] [fused-GEMM flags: 2 phases x 8 ranks x u32]
-    [fused-GEMM arrival counters: 2 x u32] [partial slot 0: T_max x H bf16] [partial slot 1]
+    [flags: 2 phases x 256 blocks x 8 ranks x u32] [fused-GEMM flags: 2 phases x 8 source ranks x
+    256 source CTAs x u32] [partial slot 0: T_max x H bf16] [partial slot 1]
     [resid: T_max x H bf16] [normed: T_max x H bf16] [push slots, parity 0 and 1: world x T_max x H]
 
 The o_proj / down_proj GEMMs write their partial sums into a partial slot; the ``ar_fused_norm``
@@ -54,8 +54,8 @@ class SymmLayout:
         row = t_max * hidden * 2
         o = 0
         off_flags = o; o = _align(o + flags_bytes)
-        off_gflags = o; o = _align(o + 2 * 8 * 4)
-        off_gcount = o; o = _align(o + 2 * 4)
+        off_gflags = o; o = _align(o + 2 * 8 * 256 * 4)
+        off_gcount = o
         off_p0 = o; o = _align(o + row)
         off_p1 = o; o = _align(o + row)
         off_resid = o; o = _align(o + row)

@@ -82,34 +82,38 @@ def test_single_slot_protocol_is_caught():
 # The decode GEMM with the all-reduce in its own launch (gemm_tcgen05.cu, ar_tail).
 #
 # Per rank, launch i runs `ctas` CTAs at once; each CTA pushes its part of every token row into
-# the owner rank's push slot (i % slots) and arrives on phase 0 (the last local arrival raises the
-# rank's phase-0 flag = i + 1 everywhere). The owner's reducing CTA waits for every rank's phase-0
-# flag, reads all sources' parts of its row, writes the normed row into every rank and arrives on
-# phase 1; a rank that owns no row raises its phase-1 flag from CTA 0 right away. CTA 0 waits for
-# every rank's phase-1 flag; the launch ends when all CTAs finished, and then the next kernel (the
-# consumer) reads the normed rows before launch i + 1 starts.
+# the owner rank's push slot (i % slots), then raises its own phase-0 flag = i + 1 in every rank.
+# The owner's reducing CTA waits for the phase-0 flags of every CTA of every rank, reads all
+# sources' parts of its row, writes the normed row into every rank and raises its phase-1 flag
+# everywhere (a rank that owns no row has no reducing CTA and raises nothing). CTA 0 waits for the
+# phase-1 flags of every rank's reducing CTAs; the launch ends when all CTAs finished, and then the
+# next kernel (the consumer) reads the normed rows before launch i + 1 starts.
 # ------------------------------------------------------------------------------------------------
 def run_gemm_ar_protocol(world, ctas, rows, calls, schedule, slots=2, wait0=True, wait1=True):
     owner_of = [r for r in range(rows)]                   # rank r owns row r (rows <= world)
     slot = [[[[-1] * ctas for _ in range(world)] for _ in range(slots)] for _ in range(world)]
     normed = [[-1] * rows for _ in range(world)]           # normed[rank][row] = call that wrote it
-    flags = [[[0] * world for _ in range(2)] for _ in range(world)]  # flags[rank][phase][src]
-    count = [[0, 0] for _ in range(world)]
+    # flags[rank][phase][src][cta] = last epoch raised there
+    flags = [[[[0] * ctas for _ in range(world)] for _ in range(2)] for _ in range(world)]
     reading_slot = [set() for _ in range(world)]           # slots a rank's reducer is reading
     reading_normed = [False] * world
     call = [0] * world
     progs, pcs = {}, {}
+    reducers = lambda r: 1 if r < rows else 0  # noqa: E731  (one reducing CTA per owned row here)
 
     def program(r, c):
-        p = [("push",), ("arrive", 0)]
-        owns = r < rows
-        if c == 0 and owns:
-            p += ([("wait", 0)] if wait0 else []) + [("read_start",), ("read_end",), ("write_normed",), ("arrive", 1)]
-        if c == 0 and not owns:
-            p += [("signal", 1)]
+        p = [("push",), ("signal", 0)]
+        if c < reducers(r):
+            p += ([("wait", 0)] if wait0 else []) + [("read_start",), ("read_end",), ("write_normed",),
+                                                   ("signal", 1)]
         if c == 0:
             p += [("wait", 1)] if wait1 else []
         return p
+
+    def ready(r, phase, e):
+        if phase == 0:
+            return all(flags[r][0][src][c] >= e for src in range(world) for c in range(ctas))
+        return all(flags[r][1][src][c] >= e for src in range(world) for c in range(reducers(src)))
 
     def start_launch(r):
         for c in range(ctas):
@@ -136,8 +140,7 @@ def run_gemm_ar_protocol(world, ctas, rows, calls, schedule, slots=2, wait0=True
         for key in live:
             op = progs[key][pcs[key]]
             r = key[0]
-            e = call[r] + 1
-            if op[0] == "wait" and min(flags[r][op[1]]) < e:
+            if op[0] == "wait" and not ready(r, op[1], call[r] + 1):
                 continue
             movable.append(key)
         if not movable:
@@ -154,17 +157,9 @@ def run_gemm_ar_protocol(world, ctas, rows, calls, schedule, slots=2, wait0=True
                 if s in reading_slot[d]:
                     return f"rank {r} cta {c} pushes call {i} into slot {s} of rank {d} during its read"
                 slot[d][s][r][c] = i
-        elif op[0] == "arrive":
-            ph = op[1]
-            count[r][ph] += 1
-            expect = ctas if ph == 0 else 1
-            if count[r][ph] == expect:
-                count[r][ph] = 0
-                for d in range(world):
-                    flags[d][ph][r] = e
         elif op[0] == "signal":
             for d in range(world):
-                flags[d][op[1]][r] = e
+                flags[d][op[1]][r][c] = e
         elif op[0] == "read_start":
             for src in range(world):
                 for cc in range(ctas):

@@ -34,7 +34,11 @@ def _run(fn, world, *args):
     import torch.multiprocessing as mp
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_entry, args=(world, port, fn, d, args), nprocs=world, join=True)
+        crash = None
+        try:
+            mp.spawn(_entry, args=(world, port, fn, d, args), nprocs=world, join=True)
+        except mp.ProcessExitedException as e:  # report the ranks' own errors, if any, with the crash
+            crash = str(e)
         errs, skips = [], []
         for r in range(world):
             f = os.path.join(d, f"err{r}")
@@ -43,7 +47,7 @@ def _run(fn, world, *args):
             f = os.path.join(d, f"skip{r}")
             if os.path.exists(f):
                 skips.append(open(f).read())
-        assert not errs, "\n".join(errs)
+        assert not errs and crash is None, "\n".join(errs + ([crash] if crash else []))
         if skips:
             pytest.skip(skips[0])
 
