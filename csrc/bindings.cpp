@@ -33,6 +33,10 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Ten
 void attn_prefill(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache, const at::Tensor& cu_q,
                   const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
                   double scale, int64_t window);
+void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache, const at::Tensor& cu_q,
+                     const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
+                     double scale, int64_t window, at::Tensor& err);
+bool attn_prefill_tc_supported(int64_t head_dim, int64_t page_size, int64_t group);
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
                    const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
@@ -69,6 +73,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode_tc", &mesh::attn_decode_tc, "paged GQA decode attention, TMA-streamed tensor-core variant");
   m.def("attn_decode_pick_splits", &mesh::attn_decode_pick_splits, "split-KV heuristic");
   m.def("attn_prefill", &mesh::attn_prefill, "paged causal varlen GQA prefill attention");
+  m.def("attn_prefill_tc", &mesh::attn_prefill_tc,
+        "paged causal varlen GQA prefill attention on tcgen05 (TMEM scores and accumulator, TMA page loads)");
+  m.def("attn_prefill_tc_supported", &mesh::attn_prefill_tc_supported, "shapes the tcgen05 prefill attention serves");
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");
   m.def("ar_barrier", &mesh::ar_barrier, "bounded cross-rank barrier over peer flags");
   m.def("ar_flags_bytes", &mesh::ar_flags_bytes, "bytes of the flag region of the AR workspace");

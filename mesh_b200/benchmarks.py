@@ -153,6 +153,58 @@ def prefill(args):
     mdist.shutdown()
 
 
+# ------------------------------------------------------------------------------------ prefill attention
+def attnprefill(args):
+    """Device time of causal paged prefill attention on one GPU for the shapes of one rank
+    (Llama-3-8B heads at --tp): batches of sequences of one length, KV read in place from shuffled
+    16-token pages. Kernels: the tcgen05 kernel ("tc"), the mma.sync kernel ("fa2") and, as a
+    library reference, torch SDPA over the same K/V gathered into contiguous [S, H, L, D] (gather
+    not timed). Reported as causal TFLOP/s (4 * L^2 / 2 * D per head) and its fraction of the
+    measured bf16 peak."""
+    import math
+    import torch
+    import torch.nn.functional as F
+    from . import ops
+    from .utils.opbench import peaks, timeit
+    _, tf, src = peaks()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hq, hkv, D, ps = 32 // args.tp, 8 // args.tp, 128, 16
+    for spec in args.shapes:
+        nseq, L = (int(x) for x in spec.split("x"))
+        pp = (L + ps - 1) // ps
+        npages = nseq * pp + 1
+        kc = torch.randn(npages, hkv, ps, D, device=dev).to(torch.bfloat16)
+        vc = torch.randn(npages, hkv, ps, D, device=dev).to(torch.bfloat16)
+        bt = (torch.randperm(npages - 1, device=dev) + 1)[:nseq * pp].view(nseq, pp).int().contiguous()
+        q = torch.randn(nseq * L, hq * D, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        cu = torch.arange(0, nseq + 1, device=dev, dtype=torch.int32) * L
+        kl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
+        flops = 4.0 * nseq * hq * D * L * L / 2
+        row = {"shape": f"{nseq}x{L} causal hq={hq} hkv={hkv} D={D}", "peak_source": src}
+        iters = max(3, min(20, int(2e12 / flops)))
+        for impl in args.impls:
+            us = timeit(lambda i: ops.attn_prefill(q, kc, vc, cu, kl, bt, out, L, 1 / math.sqrt(D), impl=impl),
+                        iters=iters)
+            ops.scratch(dev).check(f"attn_prefill[{impl}]")
+            row[f"{impl}_us"] = round(us, 1)
+            row[f"{impl}_tflops"] = round(flops / us / 1e6, 1)
+            row[f"{impl}_frac_of_measured_peak"] = round(flops / us / 1e6 / tf, 3)
+        if not args.no_sdpa:
+            kk = kc[bt.long()].permute(0, 2, 1, 3, 4).reshape(nseq, hkv, pp * ps, D)[:, :, :L]
+            vv = vc[bt.long()].permute(0, 2, 1, 3, 4).reshape(nseq, hkv, pp * ps, D)[:, :, :L]
+            kk = kk.repeat_interleave(hq // hkv, dim=1).contiguous()
+            vv = vv.repeat_interleave(hq // hkv, dim=1).contiguous()
+            qq = q.view(nseq, L, hq, D).transpose(1, 2).contiguous()
+            us = timeit(lambda i: F.scaled_dot_product_attention(qq, kk, vv, is_causal=True), iters=iters)
+            row["torch_sdpa_us"] = round(us, 1)
+            row["torch_sdpa_tflops"] = round(flops / us / 1e6, 1)
+            del kk, vv, qq
+        print(json.dumps(row), flush=True)
+        del kc, vc, q, out
+
+
 # ------------------------------------------------------------------------------------ all-reduce sweep
 def allreduce(args):
     """Per-call device time of the fused all-reduce + residual + RMSNorm (plain peer loads and NVLS
@@ -447,6 +499,11 @@ def main():
     c3.add_argument("--chunk", type=int, default=8192)
     c3.add_argument("--steps", type=int, default=3)
     c3.add_argument("--warmup", type=int, default=2)
+    c7 = sub.add_parser("attnprefill")
+    c7.add_argument("--shapes", nargs="+", default=["8x512", "64x512", "1x2048", "1x8192", "1x32768"])
+    c7.add_argument("--tp", type=int, default=1)
+    c7.add_argument("--impls", nargs="+", default=["tc", "fa2"])
+    c7.add_argument("--no-sdpa", action="store_true")
     c5 = sub.add_parser("allreduce")
     c5.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 4096, 8192])
     c5.add_argument("--hidden", type=int, nargs="+", default=[4096, 8192])
@@ -464,7 +521,7 @@ def main():
     c4.add_argument("--layers", type=int, default=0)
     a = ap.parse_args()
     {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b,
-     "gemmar": gemmar}[a.cmd](a)
+     "gemmar": gemmar, "attnprefill": attnprefill}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -245,9 +245,23 @@ def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, wi
     return out
 
 
+# MESH_PREFILL_ATTN=fa2 selects the mma.sync kernel (A/B measurements); the default is the tcgen05
+# kernel wherever it serves the shape (head_dim 128, 16-token pages)
+_PREFILL_IMPL = os.environ.get("MESH_PREFILL_ATTN", "tc")
+
+
 def attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len: int, scale: float,
-                 window: int = 0):
-    ext().attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len, scale, window)
+                 window: int = 0, impl: Optional[str] = None):
+    """Causal paged varlen GQA attention of the new tokens of each sequence. impl: "tc" (tcgen05
+    with TMEM accumulators; head_dim 128 and 16-token pages) or "fa2" (mma.sync, any page size)."""
+    impl = impl or _PREFILL_IMPL
+    D = kcache.shape[3]
+    G = (q.shape[1] // D) // kcache.shape[1]
+    if impl == "tc" and ext().attn_prefill_tc_supported(D, kcache.shape[2], G):
+        ext().attn_prefill_tc(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len, scale, window,
+                              scratch(q.device).err)
+    else:
+        ext().attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len, scale, window)
     _count()
     return out
 

@@ -23,6 +23,7 @@ ext_modules = [
             "csrc/kernels/elementwise.cu",
             "csrc/kernels/attn_decode.cu",
             "csrc/kernels/attn_prefill.cu",
+            "csrc/kernels/attn_prefill_tc.cu",
             "csrc/kernels/allreduce.cu",
         ],
         include_dirs=[os.path.join(ROOT, "csrc", "include")],

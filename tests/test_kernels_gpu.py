@@ -323,25 +323,63 @@ def test_attn_decode(G, D, impl, splits, window):
         assert rel_err(out[i].view(1, hq, D), want) < 2e-2, (i, L)
 
 
-@pytest.mark.parametrize("G", [4, 8, 1])
+@pytest.mark.parametrize("G", [4, 8, 1, 2])
 @pytest.mark.parametrize("window", [0, 50])
-def test_attn_prefill_varlen_prefix(G, window):
+@pytest.mark.parametrize("impl", ["tc", "fa2"])
+def test_attn_prefill_varlen_prefix(G, window, impl):
+    _prefill_case(G, window, impl, k_lens=[40, 300, 129, 64], q_lens=[40, 100, 1, 64], seed=40)
+
+
+@pytest.mark.parametrize("G", [4, 8])
+@pytest.mark.parametrize("q_mult", [1.0, 12.0])
+def test_attn_prefill_tc_long_blocks(G, q_mult):
+    """Several 128-key blocks per query tile, ragged ends, a cached prefix, and (q_mult 12) scores
+    spread wide enough that the running maximum moves by more than 2^8 and O is rescaled in TMEM."""
+    _prefill_case(G, 0, "tc", k_lens=[1500, 777, 256], q_lens=[700, 777, 129], seed=50, q_mult=q_mult)
+
+
+def _prefill_case(G, window, impl, k_lens, q_lens, seed, q_mult=1.0):
     hkv, D, ps = 2, 128, 16
     hq = hkv * G
-    k_lens = [40, 300, 129, 64]
-    q_lens = [40, 100, 1, 64]   # seq 1 and 2 have cached prefixes
-    kc, vc, bt, ks, vs = _paged_kv(k_lens, hkv, D, ps, seed=40)
+    kc, vc, bt, ks, vs = _paged_kv(k_lens, hkv, D, ps, seed=seed)
     T = sum(q_lens)
-    q = _rand(T, hq * D, seed=41)
-    out = torch.empty_like(q)
+    q = (_rand(T, hq * D, seed=seed + 1).float() * q_mult).to(torch.bfloat16)
+    out = torch.full_like(q, float("nan"))
     cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device=DEV)
     scale = 1 / math.sqrt(D)
     ops.attn_prefill(q, kc, vc, cu, torch.tensor(k_lens, dtype=torch.int32, device=DEV), bt, out, max(q_lens), scale,
-                     window)
+                     window, impl=impl)
     torch.cuda.synchronize()
+    ops.scratch(DEV).check("attn_prefill")
     for i, (kl, ql) in enumerate(zip(k_lens, q_lens)):
         a = int(cu[i])
         qpos = torch.arange(kl - ql, kl, device=DEV)
         want = ref.attention(q[a:a + ql].view(ql, hq, D), ks[i], vs[i], qpos, torch.arange(kl, device=DEV), scale,
                              window)
+        assert torch.isfinite(out[a:a + ql].float()).all(), (i, "rows not written")
         assert rel_err(out[a:a + ql].view(ql, hq, D), want) < 2e-2, i
+
+
+@pytest.mark.parametrize("impl", ["tc", "fa2"])
+def test_attn_prefill_batch_invariant(impl):
+    """A sequence's prefill attention output does not depend on the other sequences of the batch:
+    each sequence alone gives bitwise the same rows as the batch."""
+    hkv, D, ps, G = 2, 128, 16, 4
+    hq = hkv * G
+    k_lens, q_lens = [5, 300, 17, 140], [5, 40, 17, 140]
+    kc, vc, bt, ks, vs = _paged_kv(k_lens, hkv, D, ps, seed=60)
+    T = sum(q_lens)
+    q = _rand(T, hq * D, seed=61)
+    cu = [0] + torch.tensor(q_lens).cumsum(0).tolist()
+    scale = 1 / math.sqrt(D)
+    out = torch.full_like(q, float("nan"))
+    ops.attn_prefill(q, kc, vc, torch.tensor(cu, dtype=torch.int32, device=DEV),
+                     torch.tensor(k_lens, dtype=torch.int32, device=DEV), bt, out, max(q_lens), scale, 0, impl=impl)
+    for i, (kl, ql) in enumerate(zip(k_lens, q_lens)):
+        qi = q[cu[i]:cu[i] + ql].clone()
+        oi = torch.full_like(qi, float("nan"))
+        ops.attn_prefill(qi, kc, vc, torch.tensor([0, ql], dtype=torch.int32, device=DEV),
+                         torch.tensor([kl], dtype=torch.int32, device=DEV), bt[i:i + 1].contiguous(), oi, ql, scale,
+                         0, impl=impl)
+        torch.cuda.synchronize()
+        assert torch.equal(oi, out[cu[i]:cu[i] + ql]), (impl, i)
