@@ -4,8 +4,9 @@
 // symmetric workspace (one allocation per rank, mapped into every peer). This kernel then
 //   one-shot: every rank reads all peers' partials for every row, adds the residual, applies
 //             RMSNorm and writes resid/normed locally (latency-optimal for decode-sized T);
-//   two-shot: rank r reduces only its 1/n share of the rows, then pushes the updated residual
-//             and normed rows into every peer's workspace (P2P stores) and signals completion
+//   two-shot: rank r reduces only its 1/n share of the rows, keeps the updated residual rows
+//             (only their owner reads them in the later layers of the step), pushes the normed
+//             rows into every peer's workspace (P2P or multicast stores) and signals completion
 //             (bandwidth-optimal for prefill-sized T).
 // Replaces the reference's host-staged TCP ring all-reduce (ring_allreduce.rs:1029-1119 and the
 // device->host->device chunk copies of runtime.rs:715-752) and its separate residual add/norm.
@@ -179,6 +180,7 @@ __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long ro
   const uint64_t db = dst_rank < 0 ? a.mc : a.base[dst_rank];
   __nv_bfloat16* resid = reinterpret_cast<__nv_bfloat16*>(db + a.off_resid);
   __nv_bfloat16* normed = reinterpret_cast<__nv_bfloat16*>(db + a.off_normed);
+  uint4* resid_l = reinterpret_cast<uint4*>(a.base[a.rank] + a.off_resid);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * AR_THREADS;
@@ -195,11 +197,13 @@ __device__ __forceinline__ void store_row(const ArArgs& a, int dst_rank, long ro
         rou[j] = pack_bf16x2(x[i][2 * j], x[i][2 * j + 1]);
         nou[j] = pack_bf16x2(x[i][2 * j] * inv * g0, x[i][2 * j + 1] * inv * g1);
       }
+      // the residual row stays with the rank that reduced it (only that rank reads it in later
+      // layers of the same step); the normed row goes wherever the next GEMM runs
       if (dst_rank < 0) {
-        multimem_st_16(resid + row * a.H + v * 8, ro);
+        resid_l[row * a.H / 8 + v] = ro;
         multimem_st_16(normed + row * a.H + v * 8, no);
       } else {
-        *reinterpret_cast<uint4*>(resid + row * a.H + v * 8) = ro;
+        if (dst_rank == a.rank) *reinterpret_cast<uint4*>(resid + row * a.H + v * 8) = ro;
         *reinterpret_cast<uint4*>(normed + row * a.H + v * 8) = no;
       }
     }
@@ -279,15 +283,9 @@ __device__ __forceinline__ void warp_reduce_norm_row(const ArArgs& a, long row, 
         ss += r0 * r0 + r1 * r1;
       }
       const int c = c0 + u * 32;
-      if (TWO_SHOT && MC) {
-        multimem_st_16(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.mc + a.off_resid) + row * a.H) + c, o);
-        resid_l[c] = o;  // the pass below re-reads it locally before the multicast lands
-      } else if (TWO_SHOT) {
-        for (int q = 0; q < a.world; ++q)
-          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.base[q] + a.off_resid) + row * a.H)[c] = o;
-      } else {
-        resid_l[c] = o;
-      }
+      // two-shot too: the residual row stays local (only its owner reads it in later layers of
+      // the same step), so only the normed rows are all-gathered
+      resid_l[c] = o;
     }
   }
 #pragma unroll

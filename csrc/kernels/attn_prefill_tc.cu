@@ -1,8 +1,12 @@
 // Paged, causal, varlen GQA prefill attention on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA owns two 128-row query tiles (t = 0, 1). A row is (token, query head of the KV group), so
-// a tile is 128 / G tokens x the G query heads of one KV head and every K/V block fetched from the
-// page pool serves the whole GQA group and both tiles. Roles (320 threads):
+// Persistent: one CTA per SM walks the work items, each a pair of 128-row query tiles (t = 0, 1) of
+// one sequence and KV head, heaviest (latest) tile pairs first. A row is (token, query head of the KV
+// group), so a tile is 128 / G tokens x the G query heads of one KV head and every K/V block fetched
+// from the page pool serves the whole GQA group and both tiles. The K/V ring, the barrier phases and
+// TMEM carry over from item to item: the next item's query tiles load as soon as the last QK of the
+// current one is done, and its first QK runs while the current item's output is read out of TMEM.
+// Roles (320 threads):
 //   warp 0      TMA producer: the two query tiles (3D boxes, one per 64-dim half) and, per 128-key
 //               block, the 8 pages of K and of V (16x64 boxes, 128-byte swizzle) into a 2-stage ring;
 //   warp 1      tcgen05.mma issuer (one thread): S_t = Q_t K_j^T into the TMEM score buffer of
@@ -58,16 +62,16 @@ struct Args {
   const int* k_lens;        // [S]
   const int* block_tables;  // [S, max_pages]
   __nv_bfloat16* out;       // [T, hq*D]
-  int max_pages, hkv, hq, n_ctas;
+  int max_pages, hkv, hq, n_ctas, nseq;
   float scale_log2;
   int window;
   int* err;
 };
 
 struct Bars {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
-  uint64_t s_full[NT], p_full[NT], o_done[NT];
+  uint64_t s_full[NT], p_full[NT], o_done[NT], o_free[NT];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -77,7 +81,7 @@ constexpr size_t smem_bytes() { return 1024 + NT * TILE_BYTES + 2 * STAGES * TIL
 
 __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
   int ok = 1;
-  if (lane_id() == 0) ok = mbar_wait_bounded(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS);
+  if (lane_id() == 0) ok = mbar_wait_bounded_sleep(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -125,14 +129,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   Bars* bars = reinterpret_cast<Bars*>(v_sm + STAGES * TILE_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seq = blockIdx.z, h = blockIdx.y;
-  // the latest (longest) query tiles start first
-  Geo<G> g;
-  if (!g.init(a, seq, a.n_ctas - 1 - (int)blockIdx.x)) return;
-  const int nblk = g.nblk_all();
+  // Work item w -> (query tile pair counted from the end, KV head, sequence): every head and
+  // sequence of the latest (longest) tile pair first, so the heaviest items start first.
+  const int per = a.hkv * a.nseq;
+  const int W = a.n_ctas * per;
+  auto item = [&](int w, Geo<G>& g, int& h, int& seq) -> bool {
+    const int x = w / per, r = w - x * per;
+    h = r % a.hkv;
+    seq = r / a.hkv;
+    return g.init(a, seq, a.n_ctas - 1 - x);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->v_full[i], 1);
@@ -142,6 +152,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bars->s_full[t], 1);
       mbar_init(&bars->p_full[t], 128);
       mbar_init(&bars->o_done[t], 1);
+      mbar_init(&bars->o_free[t], 128);
     }
     mbar_init(&bars->mma_done, 1);
     bars->abort = 0;
@@ -168,63 +179,77 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
       const uint64_t pol = policy_evict_last();  // K/V pages are re-read by the other query tiles
-      const int* bt = a.block_tables + (long)seq * a.max_pages;
-      const int npages = (g.klen + PAGE - 1) / PAGE;
       griddep_wait();  // Q and the K/V pages come from the previous kernel
-      const int ntiles = g.nblk[1] > 0 ? 2 : 1;
-      mbar_arrive_expect_tx(&bars->q_full, ntiles * TILE_BYTES);
-      for (int t = 0; t < ntiles; ++t) {
-        uint8_t* qd = q_sm + t * TILE_BYTES;
-        const int tok = g.q0 + g.tok0 + t * BQT;
-        tma_load_3d(qd, &tmQ, &bars->q_full, 0, h * G, tok, pol);
-        tma_load_3d(qd + ATOM_BYTES, &tmQ, &bars->q_full, 64, h * G, tok, pol);
-      }
-      int issued = 0;
+      uint32_t kvc = 0;  // key blocks loaded so far (ring position)
+      int ic = 0;        // items started
       bool ok = true;
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-        if (!mbar_wait_bounded(&bars->kv_empty[s], ph ^ 1u, a.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag,
-                               WAIT_LIMIT_NS)) {
+      for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+        Geo<G> g;
+        int h, seq;
+        if (!item(w, g, h, seq)) continue;
+        // the query buffers are free once every QK of the previous item is done
+        if (ic > 0 && !mbar_wait_bounded_sleep(&bars->q_empty, (uint32_t)(ic - 1) & 1u, a.err,
+                                               ERR_MBAR_TIMEOUT_PRODUCER, abort_flag, WAIT_LIMIT_NS)) {
           ok = false;
           break;
         }
-        const int kb = g.kb_first + j;
-        int rows[PAGES_PER_BLOCK];
-#pragma unroll
-        for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
-          // pages past the sequence end repeat its last page: finite data under masked scores
-          const int pg = min(kb * PAGES_PER_BLOCK + p, npages - 1);
-          rows[p] = (bt[pg] * a.hkv + h) * PAGE;
+        const int ntiles = g.nblk[1] > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(&bars->q_full, ntiles * TILE_BYTES);
+        for (int t = 0; t < ntiles; ++t) {
+          uint8_t* qd = q_sm + t * TILE_BYTES;
+          const int tok = g.q0 + g.tok0 + t * BQT;
+          tma_load_3d(qd, &tmQ, &bars->q_full, 0, h * G, tok, pol);
+          tma_load_3d(qd + ATOM_BYTES, &tmQ, &bars->q_full, 64, h * G, tok, pol);
         }
-        uint8_t* kd = k_sm + s * TILE_BYTES;
-        uint8_t* vd = v_sm + s * TILE_BYTES;
-        mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
+        ++ic;
+        const int* bt = a.block_tables + (long)seq * a.max_pages;
+        const int npages = (g.klen + PAGE - 1) / PAGE;
+        const int nblk = g.nblk_all();
+        for (int j = 0; j < nblk; ++j, ++kvc) {
+          const int s = kvc % STAGES;
+          const uint32_t ph = (kvc / STAGES) & 1u;
+          if (!mbar_wait_bounded_sleep(&bars->kv_empty[s], ph ^ 1u, a.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag,
+                                       WAIT_LIMIT_NS)) {
+            ok = false;
+            break;
+          }
+          const int kb = g.kb_first + j;
+          int rows[PAGES_PER_BLOCK];
 #pragma unroll
-        for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
-          tma_load_2d(kd + p * BOX_BYTES, &tmK, &bars->k_full[s], 0, rows[p], pol);
-          tma_load_2d(kd + ATOM_BYTES + p * BOX_BYTES, &tmK, &bars->k_full[s], 64, rows[p], pol);
-        }
-        mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
+          for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
+            // pages past the sequence end repeat its last page: finite data under masked scores
+            const int pg = min(kb * PAGES_PER_BLOCK + p, npages - 1);
+            rows[p] = (bt[pg] * a.hkv + h) * PAGE;
+          }
+          uint8_t* kd = k_sm + s * TILE_BYTES;
+          uint8_t* vd = v_sm + s * TILE_BYTES;
+          mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
 #pragma unroll
-        for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
-          tma_load_2d(vd + p * BOX_BYTES, &tmV, &bars->v_full[s], 0, rows[p], pol);
-          tma_load_2d(vd + ATOM_BYTES + p * BOX_BYTES, &tmV, &bars->v_full[s], 64, rows[p], pol);
+          for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
+            tma_load_2d(kd + p * BOX_BYTES, &tmK, &bars->k_full[s], 0, rows[p], pol);
+            tma_load_2d(kd + ATOM_BYTES + p * BOX_BYTES, &tmK, &bars->k_full[s], 64, rows[p], pol);
+          }
+          mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
+#pragma unroll
+          for (int p = 0; p < PAGES_PER_BLOCK; ++p) {
+            tma_load_2d(vd + p * BOX_BYTES, &tmV, &bars->v_full[s], 0, rows[p], pol);
+            tma_load_2d(vd + ATOM_BYTES + p * BOX_BYTES, &tmV, &bars->v_full[s], 64, rows[p], pol);
+          }
         }
-        ++issued;
       }
       if (!ok) {
         // let copies already in flight land before the CTA exits (bounded)
         const uint64_t t0 = globaltimer_ns();
-        for (int j = max(0, issued - STAGES); j < issued; ++j) {
-          const int s = j % STAGES;
-          const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+        for (uint32_t k = kvc > STAGES ? kvc - STAGES : 0; k < kvc; ++k) {
+          const int s = k % STAGES;
+          const uint32_t ph = (k / STAGES) & 1u;
           while (!(mbar_try_wait(&bars->k_full[s], ph) && mbar_try_wait(&bars->v_full[s], ph)) &&
                  globaltimer_ns() - t0 < 50000000ull) {
           }
         }
-        while (!mbar_try_wait(&bars->q_full, 0) && globaltimer_ns() - t0 < 50000000ull) {
-        }
+        if (ic > 0)
+          while (!mbar_try_wait(&bars->q_full, (uint32_t)(ic - 1) & 1u) && globaltimer_ns() - t0 < 50000000ull) {
+          }
       }
     }
     __syncwarp();
@@ -236,8 +261,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return wait_warp(bar, parity, a.err, ERR_MBAR_TIMEOUT_MMA, abort_flag);
     };
-    auto issue_qk = [&](int t, int j) {
-      const int s = j % STAGES;
+    int qk_left = 0;  // QKs of the current item still to issue (the last one frees the query buffers)
+    auto issue_qk = [&](int t, int s) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -246,11 +271,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16(tmem + (uint32_t)(t * BK), ad, bd, IDESC_QK, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full[t]);
+        if (--qk_left == 0) umma_commit(&bars->q_empty);
       }
       __syncwarp();
     };
-    auto issue_pv = [&](int t, int j) {
-      const int s = j % STAGES;
+    auto issue_pv = [&](int t, int s, bool first) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
@@ -258,51 +283,82 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // of the page layout, the two 64-dim halves ATOM_BYTES apart
           const uint64_t bd = make_sdesc_sw128_mn(v_addr + s * TILE_BYTES + kk * 2048, ATOM_BYTES, 1024);
           umma_bf16_ts(tmem + O_COL + (uint32_t)(t * D), tmem + (uint32_t)(t * BK + kk * 8), bd, IDESC_PV,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+                       (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->o_done[t]);
       }
       __syncwarp();
     };
-    bool ok = wait(&bars->q_full, 0) && wait(&bars->k_full[0], 0);
-    if (ok) {
+    uint32_t kvc = 0;
+    int ic = 0;
+    int tcnt[NT] = {0, 0};  // blocks each tile has gone through (phase of s_full / p_full / o_done)
+    int tuse[NT] = {0, 0};  // items each tile has finished (phase of o_free)
+    bool ok = true;
+    for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+      Geo<G> g;
+      int h, seq;
+      if (!item(w, g, h, seq)) continue;
+      const int nblk = g.nblk_all();
+      qk_left = g.nblk[0] + g.nblk[1];
+      if (!wait(&bars->q_full, (uint32_t)ic & 1u) ||
+          !wait(&bars->k_full[kvc % STAGES], (kvc / STAGES) & 1u)) {
+        ok = false;
+        break;
+      }
+      ++ic;
       tc_fence_after();
-      for (int t = 0; t < NT; ++t)
-        if (g.nblk[t] > 0) issue_qk(t, 0);
-    }
-    for (int j = 0; j < nblk && ok; ++j) {
-      const int s = j % STAGES;
-      const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-      if (!wait(&bars->v_full[s], ph)) {
-        ok = false;
-        break;
-      }
-      const bool next = j + 1 < nblk;
-      if (next && !wait(&bars->k_full[(j + 1) % STAGES], (uint32_t)((j + 1) / STAGES) & 1u)) {
-        ok = false;
-        break;
-      }
       for (int t = 0; t < NT && ok; ++t) {
-        if (j >= g.nblk[t]) continue;
-        // softmax of tile t wrote P_t(j) into TMEM and rescaled O_t
-        if (!wait(&bars->p_full[t], (uint32_t)j & 1u)) {
+        if (g.nblk[t] == 0) continue;
+        // S_t / P_t of the previous item are free once its last PV_t is done
+        if (tcnt[t] > 0 && !wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        issue_pv(t, j);
-        if (j + 1 < g.nblk[t]) {
-          // S_t(j+1) overwrites the columns P_t(j) is read from: wait until PV_t(j) is done
-          if (!wait(&bars->o_done[t], (uint32_t)j & 1u)) {
+        issue_qk(t, kvc % STAGES);
+      }
+      for (int j = 0; j < nblk && ok; ++j) {
+        const uint32_t k = kvc + j;
+        const int s = k % STAGES;
+        if (!wait(&bars->v_full[s], (k / STAGES) & 1u)) {
+          ok = false;
+          break;
+        }
+        if (j + 1 < nblk && !wait(&bars->k_full[(k + 1) % STAGES], ((k + 1) / STAGES) & 1u)) {
+          ok = false;
+          break;
+        }
+        for (int t = 0; t < NT && ok; ++t) {
+          if (j >= g.nblk[t]) continue;
+          // softmax of tile t wrote P_t(j) into TMEM and rescaled O_t
+          if (!wait(&bars->p_full[t], (uint32_t)tcnt[t] & 1u)) {
+            ok = false;
+            break;
+          }
+          // O_t was read out by the previous item's epilogue
+          if (j == 0 && tuse[t] > 0 && !wait(&bars->o_free[t], (uint32_t)(tuse[t] - 1) & 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_qk(t, j + 1);
+          issue_pv(t, s, j == 0);
+          ++tcnt[t];
+          if (j + 1 < g.nblk[t]) {
+            // S_t(j+1) overwrites the columns P_t(j) is read from: wait until PV_t(j) is done
+            if (!wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(t, (k + 1) % STAGES);
+          }
         }
+        if (ok && lane == 0) umma_commit(&bars->kv_empty[s]);
+        __syncwarp();
       }
-      if (ok && lane == 0) umma_commit(&bars->kv_empty[s]);
-      __syncwarp();
+      kvc += nblk;
+      for (int t = 0; t < NT; ++t)
+        if (g.nblk[t] > 0) ++tuse[t];
     }
     // every MMA issued above has completed before TMEM is released
     if (lane == 0) {
@@ -317,87 +373,97 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int t = (warp - 2) >> 2;  // query tile of this warp
     const int quarter = warp & 3;   // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int nb = g.nblk[t];
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + (uint32_t)(t * BK);
     const uint32_t o_addr = tmem + lane_off + O_COL + (uint32_t)(t * D);
-    const int ttok0 = g.tok0 + t * BQT;            // first token of this tile
-    const int tq = ttok0 + row / G;
-    const int qpos = g.pos_base + tq;
-    const int lim = min(qpos, g.klen - 1);                       // last key this row may attend
-    const int low = a.window > 0 ? qpos - a.window + 1 : 0;      // first key this row may attend
-    const int tlast = min(ttok0 + BQT, g.qlen) - 1;
-    const int lim_min = min(g.pos_base + ttok0, g.klen - 1);     // smallest `lim` of the tile
-    const int low_max = a.window > 0 ? g.pos_base + tlast - a.window + 1 : 0;
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = nb > 0;
-    for (int j = 0; j < nb; ++j) {
-      if (!wait_warp(&bars->s_full[t], (uint32_t)j & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag)) {
+    int tcnt = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+      Geo<G> g;
+      int h, seq;
+      if (!item(w, g, h, seq)) continue;
+      const int nb = g.nblk[t];
+      if (nb == 0) continue;
+      const int ttok0 = g.tok0 + t * BQT;            // first token of this tile
+      const int tq = ttok0 + row / G;
+      const int qpos = g.pos_base + tq;
+      const int lim = min(qpos, g.klen - 1);                       // last key this row may attend
+      const int low = a.window > 0 ? qpos - a.window + 1 : 0;      // first key this row may attend
+      const int tlast = min(ttok0 + BQT, g.qlen) - 1;
+      const int lim_min = min(g.pos_base + ttok0, g.klen - 1);     // smallest `lim` of the tile
+      const int low_max = a.window > 0 ? g.pos_base + tlast - a.window + 1 : 0;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nb; ++j, ++tcnt) {
+        if (!wait_warp(&bars->s_full[t], (uint32_t)tcnt & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[BK];
+#pragma unroll
+        for (int c = 0; c < BK / 16; ++c)
+          tmem_ld16(s_addr + (uint32_t)(16 * c), *reinterpret_cast<uint32_t(*)[16]>(&sv[16 * c]));
+        tmem_ld_wait_tied(sv);
+
+        const int key0 = (g.kb_first + j) * BK;
+        if (key0 + BK - 1 > lim_min || key0 < low_max) {
+#pragma unroll
+          for (int c = 0; c < BK; ++c)
+            if (key0 + c > lim || key0 + c < low) sv[c] = __float_as_uint(-INFINITY);
+        }
+        // row maximum (raw scores; the scale is folded into the exponent below)
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
+#pragma unroll
+        for (int c = 8; c < BK; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sv[c]));
+        const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        const float m_new = fmaxf(m_used, mraw * a.scale_log2);
+        const bool resc = m_new > m_used + RESCALE_THRESHOLD;
+        float alpha = 1.f;
+        if (resc) {
+          alpha = ex2_ftz(m_used - m_new);  // 0 when m_used is -inf
+          m_used = m_new;
+        }
+        const bool dead = m_used == -INFINITY;  // nothing attended yet (window / padding rows)
+        const float mb = dead ? 0.f : m_used;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        // P_t(j) overwrites the first 64 columns of the score buffer, 16 packed columns at a time
+#pragma unroll
+        for (int c = 0; c < BK / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_ftz(fmaf(__uint_as_float(sv[32 * c + 2 * e]), a.scale_log2, -mb));
+            const float p1 = ex2_ftz(fmaf(__uint_as_float(sv[32 * c + 2 * e + 1]), a.scale_log2, -mb));
+            sum[e & 3] += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(s_addr + (uint32_t)(16 * c), pk);
+        }
+        l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+        // PV_t(j-1) finished before QK_t(j) was issued, so O_t is stable here
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t ov[16];
+            tmem_ld16(o_addr + 16 * c, ov);
+            tmem_ld_wait_tied(ov);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st16(o_addr + 16 * c, ov);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[t]);
+      }
+      if (!ok || !wait_warp(&bars->o_done[t], (uint32_t)(tcnt - 1) & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE,
+                            abort_flag)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t sv[BK];
-#pragma unroll
-      for (int c = 0; c < BK / 16; ++c)
-        tmem_ld16(s_addr + (uint32_t)(16 * c), *reinterpret_cast<uint32_t(*)[16]>(&sv[16 * c]));
-      tmem_ld_wait_tied(sv);
-
-      const int key0 = (g.kb_first + j) * BK;
-      if (key0 + BK - 1 > lim_min || key0 < low_max) {
-#pragma unroll
-        for (int c = 0; c < BK; ++c)
-          if (key0 + c > lim || key0 + c < low) sv[c] = __float_as_uint(-INFINITY);
-      }
-      // row maximum (raw scores; the scale is folded into the exponent below)
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
-#pragma unroll
-      for (int c = 8; c < BK; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sv[c]));
-      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m_used, mraw * a.scale_log2);
-      const bool resc = m_new > m_used + RESCALE_THRESHOLD;
-      float alpha = 1.f;
-      if (resc) {
-        alpha = exp2f(m_used - m_new);  // 0 when m_used is -inf
-        m_used = m_new;
-      }
-      const bool dead = m_used == -INFINITY;  // nothing attended yet (window / padding rows)
-      const float mb = dead ? 0.f : m_used;
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      // P_t(j) overwrites the first 64 columns of the score buffer, 16 packed columns at a time
-#pragma unroll
-      for (int c = 0; c < BK / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = exp2f(fmaf(__uint_as_float(sv[32 * c + 2 * e]), a.scale_log2, -mb));
-          const float p1 = exp2f(fmaf(__uint_as_float(sv[32 * c + 2 * e + 1]), a.scale_log2, -mb));
-          sum[e & 3] += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(s_addr + (uint32_t)(16 * c), pk);
-      }
-      l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
-      // PV_t(j-1) finished before QK_t(j) was issued, so O_t is stable here
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t ov[16];
-          tmem_ld16(o_addr + 16 * c, ov);
-          tmem_ld_wait_tied(ov);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st16(o_addr + 16 * c, ov);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->p_full[t]);
-    }
-    if (ok && wait_warp(&bars->o_done[t], (uint32_t)(nb - 1) & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool valid = tq < g.qlen;
@@ -421,6 +487,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           reinterpret_cast<uint4*>(dst + 16 * c)[1] = w1;
         }
       }
+      // O_t may take the next item's first PV
+      tc_fence_before();
+      mbar_arrive(&bars->o_free[t]);
     }
   }
   tc_fence_before();
@@ -475,10 +544,16 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
   a.hkv = hkv;
   a.hq = hq;
   a.n_ctas = (int)((max_q_len + NT * BQT - 1) / (NT * BQT));
+  a.nseq = S;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.window = (int)window;
   a.err = err.data_ptr<int>();
-  dim3 grid(a.n_ctas, hkv, S);
+  // persistent: one CTA per SM walks the work items (tile pair, KV head, sequence)
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device()));
+  const long items = (long)a.n_ctas * hkv * S;
+  TORCH_CHECK(items < (1l << 31), "attn_prefill_tc: too many work items");
+  dim3 grid((unsigned)std::min<long>(items, sms));
   const size_t smem = smem_bytes();
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto go = [&](auto kern) {
