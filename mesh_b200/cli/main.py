@@ -111,8 +111,8 @@ def cmd_device_init(a):
          "execution": {"preferred_provider": a.preferred_provider or ("cuda" if cap["gpus"] else "cpu")},
          "governance": {"max_concurrent_jobs": 8, "tensor_plane_max_message_bytes": 10 * 1024 * 1024,
                         "recovery_cooldown_ms": 5000, "recovery_max_loads_per_minute": 8},
-         "b200": {"tp": 1, "gpu_ids": [g for g in range(len(cap["gpus"]))], "page_tokens": 16,
-                  "max_decode_batch": 64, "cuda_graphs": True}}
+         "b200": {"tp": a.tp, "gpu_ids": [g for g in range(len(cap["gpus"]))], "page_tokens": 16,
+                  "max_decode_batch": 64, "cuda_graphs": True, "model_dir": a.model_dir or ""}}
     save_device(d)
     try:
         client(d).register(device_id=d["device_id"], network_id=a.network_id, name=a.name, tier=cap["tier"],
@@ -173,17 +173,52 @@ def build_coordinator(d: dict, model_id: str):
                                 stats=stats, worker_id=d["device_id"], model_id=model_id)
 
 
-def cmd_device_runtime(a):
+def _make_worker(d: dict, coord):
     from ..runtime.worker import Worker
+    ring = d.get("ring", {})
+    return Worker(client(d), d["device_id"], d["network_id"], ring["model_id"], coord, tier=d.get("tier", "tier2"),
+                  provider=d.get("execution", {}).get("preferred_provider", "cpu"),
+                  contributed_memory=int(ring.get("memory", 0)),
+                  heartbeat_interval_s=float(os.environ.get("MESHNET_HEARTBEAT_INTERVAL_MS", "5000")) / 1000.0)
+
+
+def _tp_group_leader(tb, cfg, ecfg, d=None):
+    """Rank 0 of a multi-GPU group: the coordinator over the group backend, driven by the worker loop."""
+    from ..engine.coordinator import InferenceCoordinator
+    from ..engine.stats import InferenceStats
+    stats = InferenceStats()
+    coord = InferenceCoordinator(tb, ecfg, stats=stats, worker_id=d["device_id"], model_id=d["ring"]["model_id"])
+    w = _make_worker(d, coord)
+    w.start()
+    try:
+        w.run()
+    finally:
+        stats.save_to_file(str(home()))
+    return {"completed": w.completed}
+
+
+def cmd_device_runtime(a):
     d = load_device()
     ring = d.get("ring", {})
     if not ring.get("model_id"):
         raise SystemExit("join a ring first: `mesh ring join --model-id <id>`")
+    b2 = d.get("b200", {})
+    tp = int(b2.get("tp", 1))
+    model_dir = b2.get("model_dir") or ""
+    if d.get("execution", {}).get("preferred_provider") == "cuda" and (tp > 1 or model_dir):
+        # one process per GPU; rank 0 runs the worker loop and drives the group
+        import functools
+        import tempfile
+        from ..runtime.tp_group import GroupSpec, run_group
+        spec = GroupSpec(world=tp, model_dir=model_dir or None, preset=None if model_dir else ring["model_id"],
+                         max_seq_len=int(b2.get("max_seq_len", 4096)), num_pages=int(b2.get("kv_pages", 4096)),
+                         max_batch=int(b2.get("max_decode_batch", 64)),
+                         use_cuda_graphs=bool(b2.get("cuda_graphs", True)))
+        with tempfile.TemporaryDirectory(dir=str(home())) as wd:
+            run_group(spec, functools.partial(_tp_group_leader, d=d), wd)
+        return
     coord = build_coordinator(d, ring["model_id"])
-    w = Worker(client(d), d["device_id"], d["network_id"], ring["model_id"], coord, tier=d.get("tier", "tier2"),
-               provider=d.get("execution", {}).get("preferred_provider", "cpu"),
-               contributed_memory=int(ring.get("memory", 0)),
-               heartbeat_interval_s=float(os.environ.get("MESHNET_HEARTBEAT_INTERVAL_MS", "5000")) / 1000.0)
+    w = _make_worker(d, coord)
     w.start()
     try:
         w.run()
@@ -417,6 +452,8 @@ def build_parser():
     i.add_argument("-c", "--control-plane", default="http://localhost:8080")
     i.add_argument("--preferred-provider", choices=["cpu", "cuda"])
     i.add_argument("--device-id")
+    i.add_argument("--tp", type=int, default=1, help="GPUs of this box that serve as one tensor-parallel group")
+    i.add_argument("--model-dir", default="", help="on-disk model (model.json + shards) the group loads")
     i.set_defaults(fn=cmd_device_init)
     s = dev.add_parser("start")
     s.add_argument("-l", "--log-level", default="info")
