@@ -37,6 +37,9 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
                      const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
                      double scale, int64_t window, at::Tensor& err);
 bool attn_prefill_tc_supported(int64_t head_dim, int64_t page_size, int64_t group);
+void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err);
+bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi);
+void kv_pages_copy(at::Tensor& k_pool, at::Tensor& v_pool, at::Tensor& buf, const at::Tensor& pages, bool to_buf);
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
                    const at::Tensor& gamma, double eps, at::Tensor& epoch, at::Tensor& err, int64_t nblocks,
@@ -76,6 +79,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill_tc", &mesh::attn_prefill_tc,
         "paged causal varlen GQA prefill attention on tcgen05 (TMEM scores and accumulator, TMA page loads)");
   m.def("attn_prefill_tc_supported", &mesh::attn_prefill_tc_supported, "shapes the tcgen05 prefill attention serves");
+  m.def("gemm_2sm", &mesh::gemm_2sm, "prefill GEMM on SM pairs (tcgen05.mma.cta_group::2, 256x256 tiles)");
+  m.def("gemm_2sm_supported", &mesh::gemm_2sm_supported, "shapes the SM-pair GEMM serves");
+  m.def("kv_pages_copy", &mesh::kv_pages_copy,
+        "gather a session's KV pages (every layer) into a contiguous buffer, or scatter one into pages");
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");
   m.def("ar_barrier", &mesh::ar_barrier, "bounded cross-rank barrier over peer flags");
   m.def("ar_flags_bytes", &mesh::ar_flags_bytes, "bytes of the flag region of the AR workspace");

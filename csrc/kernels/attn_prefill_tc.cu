@@ -34,6 +34,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "../include/launch.h"
 #include "../include/sm100.cuh"
 #include "../include/tma_host.h"
@@ -65,6 +67,7 @@ struct Args {
   int max_pages, hkv, hq, n_ctas, nseq;
   float scale_log2;
   int window;
+  int spin;  // 1: waits poll the barrier; 0: waits sleep inside try_wait between polls
   int* err;
 };
 
@@ -79,10 +82,19 @@ struct Bars {
 
 constexpr size_t smem_bytes() { return 1024 + NT * TILE_BYTES + 2 * STAGES * TILE_BYTES + sizeof(Bars); }
 
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag,
+                                          int spin) {
   int ok = 1;
-  if (lane_id() == 0) ok = mbar_wait_bounded_sleep(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS);
+  if (lane_id() == 0)
+    ok = spin ? mbar_wait_bounded(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS)
+              : mbar_wait_bounded_sleep(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ bool wait_one(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag,
+                                         int spin) {
+  return spin ? mbar_wait_bounded(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS)
+              : mbar_wait_bounded_sleep(bar, parity, err, code, abort_flag, WAIT_LIMIT_NS);
 }
 
 // Per-CTA geometry shared by every role.
@@ -188,8 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int h, seq;
         if (!item(w, g, h, seq)) continue;
         // the query buffers are free once every QK of the previous item is done
-        if (ic > 0 && !mbar_wait_bounded_sleep(&bars->q_empty, (uint32_t)(ic - 1) & 1u, a.err,
-                                               ERR_MBAR_TIMEOUT_PRODUCER, abort_flag, WAIT_LIMIT_NS)) {
+        if (ic > 0 && !wait_one(&bars->q_empty, (uint32_t)(ic - 1) & 1u, a.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag, a.spin)) {
           ok = false;
           break;
         }
@@ -208,8 +219,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j = 0; j < nblk; ++j, ++kvc) {
           const int s = kvc % STAGES;
           const uint32_t ph = (kvc / STAGES) & 1u;
-          if (!mbar_wait_bounded_sleep(&bars->kv_empty[s], ph ^ 1u, a.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag,
-                                       WAIT_LIMIT_NS)) {
+          if (!wait_one(&bars->kv_empty[s], ph ^ 1u, a.err, ERR_MBAR_TIMEOUT_PRODUCER, abort_flag, a.spin)) {
             ok = false;
             break;
           }
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr uint32_t IDESC_PV = make_idesc_bf16(BM, D) | IDESC_B_MN_MAJOR;
     const uint32_t q_addr = smem_u32(q_sm), k_addr = smem_u32(k_sm), v_addr = smem_u32(v_sm);
     auto wait = [&](uint64_t* bar, uint32_t parity) {
-      return wait_warp(bar, parity, a.err, ERR_MBAR_TIMEOUT_MMA, abort_flag);
+      return wait_warp(bar, parity, a.err, ERR_MBAR_TIMEOUT_MMA, abort_flag, a.spin);
     };
     int qk_left = 0;  // QKs of the current item still to issue (the last one frees the query buffers)
     auto issue_qk = [&](int t, int s) {
@@ -394,7 +404,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int low_max = a.window > 0 ? g.pos_base + tlast - a.window + 1 : 0;
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < nb; ++j, ++tcnt) {
-        if (!wait_warp(&bars->s_full[t], (uint32_t)tcnt & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag)) {
+        if (!wait_warp(&bars->s_full[t], (uint32_t)tcnt & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag, a.spin)) {
           ok = false;
           break;
         }
@@ -460,7 +470,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&bars->p_full[t]);
       }
       if (!ok || !wait_warp(&bars->o_done[t], (uint32_t)(tcnt - 1) & 1u, a.err, ERR_MBAR_TIMEOUT_EPILOGUE,
-                            abort_flag)) {
+                            abort_flag, a.spin)) {
         ok = false;
         break;
       }
@@ -548,6 +558,11 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.window = (int)window;
   a.err = err.data_ptr<int>();
+  static const int spin = [] {
+    const char* e = std::getenv("MESH_WAIT_SPIN");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  a.spin = spin;
   // persistent: one CTA per SM walks the work items (tile pair, KV head, sequence)
   int sms = 0;
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device()));

@@ -205,6 +205,35 @@ def attnprefill(args):
         del kc, vc, q, out
 
 
+# ------------------------------------------------------------------------------------ prefill GEMM kernels
+def gemmcmp(args):
+    """One prefill-sized product out = A @ B^T on one GPU: the SM-pair kernel, the one-SM kernel and
+    cuBLAS (torch.mm), CUDA-graph timed with B rotated past L2, as TFLOP/s and fraction of the
+    measured bf16 peak."""
+    import torch
+    from . import ops
+    from .utils.opbench import copies_for, peaks, timeit
+    _, tf, src = peaks()
+    dev = torch.device("cuda", 0)
+    M, N, K = args.M, args.N, args.K
+    nc = min(copies_for(N * K * 2), 16)
+    a = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    bs = [torch.randn(N, K, device=dev).mul_(0.02).to(torch.bfloat16) for _ in range(nc)]
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    flops = 2.0 * M * N * K
+    row = {"shape": f"M={M} N={N} K={K}", "peak_source": src}
+    runs = {"pair": lambda i: ops.gemm_pair(a, bs[i % nc], out),
+            "one_sm": lambda i: ops.gemm(a, bs[i % nc], out, ops.EPI_STORE_BF16, trans=False),
+            "cublas": lambda i: torch.mm(a, bs[i % nc].t(), out=out)}
+    for name in args.impls:
+        us = timeit(runs[name], iters=args.iters)
+        row[f"{name}_us"] = round(us, 2)
+        row[f"{name}_tflops"] = round(flops / us / 1e6, 1)
+        row[f"{name}_frac"] = round(flops / us / 1e6 / tf, 3)
+    ops.scratch(dev).check("gemmcmp")
+    print(json.dumps(row), flush=True)
+
+
 # ------------------------------------------------------------------------------------ all-reduce sweep
 def allreduce(args):
     """Per-call device time of the fused all-reduce + residual + RMSNorm (plain peer loads and NVLS
@@ -416,12 +445,12 @@ def gemmar(args):
 
 # ------------------------------------------------------------------------------------ 70B serving
 def serve70b(args):
-    """256 sessions, prompts U[128,2048], 256 output tokens; after half the decode steps 10% of
-    the sessions are handed off (KV snapshot out, session released, snapshot re-imported as a new
-    session) to exercise checkpoint-backed KV handoff between decode queues."""
+    """256 sessions, prompts U[128,2048], 256 output tokens, served by decode queue A; after half
+    the decode steps 10% of the sessions are handed off to a second decode queue B (its own engine,
+    KV pool and CUDA graphs over the same weights): each session's pages are gathered on the device,
+    re-allocated in B's pool and scattered there, and both queues keep decoding to the end."""
     di, dist, torch = _dist()
     from .config import EngineConfig, get_preset
-    from .engine.kv_snapshot import KVSequenceState, export_snapshot, import_snapshot
     from .engine.serving import Engine
     from .models.llama import KVPool, LlamaRunner
     from .models.weights import synthetic_device_weights
@@ -435,11 +464,16 @@ def serve70b(args):
     maxs = (2048 + G + 15) // 16 * 16
     ecfg = EngineConfig(tp=di.world, max_seq_len=maxs, prefill_chunk_tokens=args.chunk)
     w = synthetic_device_weights(cfg, di.rank, di.world, device=dev)
+    group = dist.group.WORLD if di.world > 1 else None
     pages = sum((l + G + 15) // 16 for l in lens) + 64
-    kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
-    runner = LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD if di.world > 1 else None,
-                         max_tokens=args.chunk + 2048)
-    eng = Engine(runner, ecfg, max_batch=S)
+    eng = Engine(LlamaRunner(w, ecfg, KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev), dev, group=group,
+                             max_tokens=args.chunk + 2048), ecfg, max_batch=S)
+    n_hand = max(1, int(args.handoff * S)) if args.handoff > 0 else 0
+    eng_b = None
+    if n_hand:
+        pages_b = sum((l + G + 15) // 16 for l in lens[:n_hand]) + 16
+        eng_b = Engine(LlamaRunner(w, ecfg, KVPool(cfg, w.layout.local_kv_heads, pages_b, 16, dev), dev, group=group,
+                                   max_tokens=max(n_hand, 64)), ecfg, max_batch=n_hand)
     prompts = [rng.integers(0, cfg.vocab_size, l).tolist() for l in lens]
     ev0, evp, evd = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     ev0.record()
@@ -449,40 +483,42 @@ def serve70b(args):
     evp.record()
     steps = 0
     handed = 0
-    while eng.has_work():
-        eng.decode_step()
+    hand_ms = 0.0
+    while eng.has_work() or (eng_b is not None and eng_b.has_work()):
+        if eng.has_work():
+            eng.decode_step()
+        if eng_b is not None and eng_b.has_work():
+            eng_b.decode_step()
         steps += 1
-        if steps == G // 2 and args.handoff > 0:
-            # mid-run handoff of a fraction of the sessions between decode queues
-            n = max(1, int(args.handoff * S))
-            for sid in sids[:n]:
-                s = eng.sessions[sid]
-                if s.status != "decoding":
+        if steps == G // 2 and n_hand:
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record()
+            for sid in sids[:n_hand]:
+                if eng.sessions[sid].status != "decoding":
                     continue
-                snap = export_snapshot(kv.k, kv.v, s.pages, KVSequenceState(0, s.kv_len, s.kv_len), cfg.name)
-                blob = snap.to_bytes()
-                eng._free_session(s)
-                from .engine.kv_snapshot import KVCacheSnapshot
-                s.pages = import_snapshot(kv.k, kv.v, eng.alloc, KVCacheSnapshot.from_bytes(blob))
-                free = eng._free_slots()
-                s.slot = free[0]
-                eng.running[s.slot] = s
-                eng.bt_host[s.slot, :len(s.pages)] = s.pages
-                eng.bt_dirty = True
+                eng_b.import_session(eng.export_session(sid))
                 handed += 1
+            h1.record()
+            torch.cuda.synchronize()
+            hand_ms = h0.elapsed_time(h1)
     evd.record()
     eng.flush_history()
+    if eng_b is not None:
+        eng_b.flush_history()
     torch.cuda.synchronize()
     dec_ms = _max_over_ranks(evp.elapsed_time(evd), dist, torch, dev)
     pre_ms = _max_over_ranks(ev0.elapsed_time(evp), dist, torch, dev)
-    ttft = sorted(ev0.elapsed_time(eng.sessions[s].ttft_event) for s in sids)
+    hand_ms = _max_over_ranks(hand_ms, dist, torch, dev)
+    ttft = sorted(ev0.elapsed_time(eng.sessions[s].ttft_event) for s in sids if s in eng.sessions)
     p50 = _max_over_ranks(ttft[len(ttft) // 2], dist, torch, dev)
     if di.rank == 0:
         print(json.dumps({"config": f"{cfg.name} tp{di.world} {S} sessions U[128,2048] x {G}",
                           "decode_tokens_per_s": S * (G - 1) / (dec_ms / 1e3), "p50_ttft_ms": p50,
                           "prefill_ms": pre_ms, "decode_ms": dec_ms, "sessions_handed_off": handed,
-                          "layers": cfg.num_layers}), flush=True)
+                          "handoff_ms": hand_ms, "layers": cfg.num_layers}), flush=True)
     eng.close()
+    if eng_b is not None:
+        eng_b.close()
     from .parallel import dist as mdist
     mdist.shutdown()
 
@@ -504,6 +540,12 @@ def main():
     c7.add_argument("--tp", type=int, default=1)
     c7.add_argument("--impls", nargs="+", default=["tc", "fa2"])
     c7.add_argument("--no-sdpa", action="store_true")
+    c8 = sub.add_parser("gemmcmp")
+    c8.add_argument("--M", type=int, default=4096)
+    c8.add_argument("--N", type=int, default=4096)
+    c8.add_argument("--K", type=int, default=4096)
+    c8.add_argument("--iters", type=int, default=20)
+    c8.add_argument("--impls", nargs="+", default=["pair", "one_sm", "cublas"])
     c5 = sub.add_parser("allreduce")
     c5.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 4096, 8192])
     c5.add_argument("--hidden", type=int, nargs="+", default=[4096, 8192])
@@ -521,7 +563,7 @@ def main():
     c4.add_argument("--layers", type=int, default=0)
     a = ap.parse_args()
     {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b,
-     "gemmar": gemmar, "attnprefill": attnprefill}[a.cmd](a)
+     "gemmar": gemmar, "attnprefill": attnprefill, "gemmcmp": gemmcmp}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -57,6 +57,27 @@ class Session:
         return self.n_generated >= self.max_new_tokens
 
 
+@dataclass
+class SessionHandoff:
+    """A decoding session lifted out of one engine: its request, the tokens so far and its KV pages
+    gathered into one device buffer ``kv`` [2, layers, pages, page_elems] (K then V). Moving it to
+    another GPU is one peer copy (``to``); ``Engine.import_session`` continues it there."""
+    prompt: List[int]
+    generated: List[int]
+    max_new_tokens: int
+    temperature: float
+    top_p: float
+    seed_base: int
+    eos_token: Optional[int]
+    kv_len: int
+    page_size: int
+    kv: torch.Tensor
+
+    def to(self, device) -> "SessionHandoff":
+        import dataclasses
+        return dataclasses.replace(self, kv=self.kv.to(device, non_blocking=True))
+
+
 class DecodeGraphs:
     """Static decode buffers shared by all buckets plus one captured graph per bucket."""
 
@@ -449,6 +470,59 @@ class Engine:
             if s.done:
                 self._retire(s)
         return n
+
+    # ----------------------------------------------------------------------------- handoff
+    def export_session(self, sid: int) -> SessionHandoff:
+        """Take a decoding session out of this engine (reference: moving a session between decode
+        queues with its KV, coordinator.rs:1916-1957). The generated tokens are read back first; the
+        session's pages are gathered on the device and then returned to this engine's pool."""
+        from .. import ops
+        s = self.sessions[sid]
+        if s.status != "decoding":
+            raise ValueError(f"session {sid} is {s.status}; only decoding sessions can be handed off")
+        self.flush_history()
+        n = (s.kv_len + self.page_size - 1) // self.page_size
+        kv = ops.kv_pages_gather(self.runner.kv.k, self.runner.kv.v, s.pages[:n])
+        h = SessionHandoff(list(s.prompt), list(s.generated), s.max_new_tokens, s.temperature, s.top_p,
+                           s.seed_base, s.eos_token, s.kv_len, self.page_size, kv)
+        # the gather is ordered before any later reuse of these pages by this engine's stream
+        self._free_session(s)
+        s.status = "handed_off"
+        del self.sessions[sid]
+        return h
+
+    def import_session(self, h: SessionHandoff) -> int:
+        """Continue a session exported by ``export_session`` (from this or another engine with the
+        same model shard geometry); returns its id here."""
+        from .. import ops
+        if h.page_size != self.page_size:
+            raise ValueError(f"handoff pages hold {h.page_size} tokens, this pool {self.page_size}")
+        L, _, hkv, ps, D = self.runner.kv.k.shape
+        n = (h.kv_len + ps - 1) // ps
+        if tuple(h.kv.shape) != (2, L, n, hkv * ps * D):
+            raise ValueError(f"handoff KV {tuple(h.kv.shape)} does not fit this pool ({L} layers, {hkv} KV heads)")
+        free = self._free_slots()
+        if not free:
+            raise RuntimeError("no free decode slot for the imported session")
+        pages = self.alloc.alloc(n) if n else []
+        if pages is None:
+            raise RuntimeError("KV page pool exhausted during import")
+        sid = self.next_sid
+        self.next_sid += 1
+        s = Session(sid, list(h.prompt), h.max_new_tokens, h.temperature, h.top_p, h.seed_base, h.eos_token,
+                    generated=list(h.generated), pages=list(pages), kv_len=h.kv_len, prefilled=len(h.prompt),
+                    n_generated=len(h.generated), status="decoding", t_submit=time.perf_counter())
+        ops.kv_pages_scatter(self.runner.kv.k, self.runner.kv.v, s.pages, h.kv.to(self.device))
+        s.slot = free[0]
+        self.running[s.slot] = s
+        self.bt_host[s.slot, :] = 0
+        self.bt_host[s.slot, :len(s.pages)] = s.pages
+        self.bt_dirty = True
+        self.dec.ids[s.slot] = int(h.generated[-1])
+        self.sessions[sid] = s
+        if s.done:
+            self._retire(s)
+        return sid
 
     def _retire(self, s: Session):
         s.status = "finished"

@@ -166,7 +166,23 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
         swap_ab = T <= SWAP_AB_MAX_TOKENS
     if swap_ab:
         return gemm(w, x, out, epi, trans=True, push=push)
+    if (not push and _PAIR_GEMM and T >= PAIR_GEMM_MIN_TOKENS and epi in (EPI_STORE_BF16, EPI_SILU_BF16)
+            and ext().gemm_2sm_supported(T, N, x.shape[1], epi)):
+        return gemm_pair(x, w, out, epi)
     return gemm(x, w, out, epi, trans=False, push=push)
+
+
+# Prefill-sized products run on SM pairs (256x256 tiles, tcgen05.mma.cta_group::2) from this many
+# tokens when MESH_PAIR_GEMM=1 (off by default until it outruns the one-SM kernel).
+PAIR_GEMM_MIN_TOKENS = 512
+_PAIR_GEMM = os.environ.get("MESH_PAIR_GEMM", "0") == "1"
+
+
+def gemm_pair(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16) -> torch.Tensor:
+    """out = x @ w.T (EPI_SILU_BF16: SiLU(gate) * up of the interleaved gate/up product) on SM pairs."""
+    ext().gemm_2sm(x, w, out, epi, scratch(x.device).err)
+    _count()
+    return out
 
 
 def add_rmsnorm(resid: torch.Tensor, gamma: torch.Tensor, normed: torch.Tensor, eps: float,
@@ -264,6 +280,33 @@ def attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len: 
         ext().attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len, scale, window)
     _count()
     return out
+
+
+def kv_pages_gather(k_pool: torch.Tensor, v_pool: torch.Tensor, pages, out: Optional[torch.Tensor] = None):
+    """[layers, pages, hkv, ps, D] pools -> buffer [2, layers, len(pages), hkv*ps*D] (K then V)."""
+    L, P = k_pool.shape[0], k_pool.shape[1]
+    _check_pages(pages, P)
+    page_elems = k_pool[0, 0].numel()
+    if out is None:
+        out = torch.empty(2, L, len(pages), page_elems, dtype=k_pool.dtype, device=k_pool.device)
+    idx = torch.tensor(list(pages), dtype=torch.int32).pin_memory().to(k_pool.device, non_blocking=True)
+    ext().kv_pages_copy(k_pool, v_pool, out, idx, True)
+    _count()
+    return out
+
+
+def kv_pages_scatter(k_pool: torch.Tensor, v_pool: torch.Tensor, pages, buf: torch.Tensor):
+    """Inverse of ``kv_pages_gather``: buffer rows go into ``pages`` of the pools (same device)."""
+    _check_pages(pages, k_pool.shape[1])
+    idx = torch.tensor(list(pages), dtype=torch.int32).pin_memory().to(k_pool.device, non_blocking=True)
+    ext().kv_pages_copy(k_pool, v_pool, buf, idx, False)
+    _count()
+
+
+def _check_pages(pages, pool_pages: int):
+    for p in pages:
+        if not 0 <= int(p) < pool_pages:
+            raise ValueError(f"page id {p} outside the pool of {pool_pages} pages")
 
 
 def argmax_partial(logits: torch.Tensor, vocab_offset: int, out: torch.Tensor):

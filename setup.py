@@ -24,6 +24,8 @@ ext_modules = [
             "csrc/kernels/attn_decode.cu",
             "csrc/kernels/attn_prefill.cu",
             "csrc/kernels/attn_prefill_tc.cu",
+            "csrc/kernels/kv_pages.cu",
+            "csrc/kernels/gemm_2sm.cu",
             "csrc/kernels/allreduce.cu",
         ],
         include_dirs=[os.path.join(ROOT, "csrc", "include")],
