@@ -37,8 +37,19 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
                      const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
                      double scale, int64_t window, at::Tensor& err);
 bool attn_prefill_tc_supported(int64_t head_dim, int64_t page_size, int64_t group);
-void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err);
+void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err,
+              const c10::optional<at::Tensor>& trace);
 bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi);
+void samp_stats(const at::Tensor& logits, const at::Tensor& inv_t, const at::Tensor& gmax, at::Tensor& out,
+                int64_t step);
+void samp_init(int64_t stage, int64_t world, int64_t rank, const at::Tensor& inv_t, const at::Tensor& top_p,
+               const at::Tensor& thr, const at::Tensor& masses, at::Tensor& st, at::Tensor& active);
+void samp_radix(const at::Tensor& logits, const at::Tensor& inv_t, const at::Tensor& gmax, at::Tensor& st,
+                at::Tensor& active, at::Tensor& hist, int64_t shift, int64_t phase);
+void samp_find(const at::Tensor& logits, const at::Tensor& inv_t, const at::Tensor& gmax, const at::Tensor& top_p,
+               const at::Tensor& thr, at::Tensor& st, at::Tensor& active, int64_t vocab_offset, at::Tensor& cand);
+void samp_merge(const at::Tensor& inv_t, const at::Tensor& top_p, const at::Tensor& cand, const at::Tensor& greedy,
+                at::Tensor& ids);
 void kv_pages_copy(at::Tensor& k_pool, at::Tensor& v_pool, at::Tensor& buf, const at::Tensor& pages, bool to_buf);
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
@@ -79,8 +90,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill_tc", &mesh::attn_prefill_tc,
         "paged causal varlen GQA prefill attention on tcgen05 (TMEM scores and accumulator, TMA page loads)");
   m.def("attn_prefill_tc_supported", &mesh::attn_prefill_tc_supported, "shapes the tcgen05 prefill attention serves");
-  m.def("gemm_2sm", &mesh::gemm_2sm, "prefill GEMM on SM pairs (tcgen05.mma.cta_group::2, 256x256 tiles)");
+  m.def("gemm_2sm", &mesh::gemm_2sm, "prefill GEMM on SM pairs (tcgen05.mma.cta_group::2, 256x256 tiles)",
+        py::arg("A"), py::arg("B"), py::arg("out"), py::arg("epi"), py::arg("err"), py::arg("trace") = py::none());
   m.def("gemm_2sm_supported", &mesh::gemm_2sm_supported, "shapes the SM-pair GEMM serves");
+  m.def("samp_stats", &mesh::samp_stats, "sampling: row max (step 0) / fixed-point mass (step 1)");
+  m.def("samp_init", &mesh::samp_init, "sampling: per-row selection set-up");
+  m.def("samp_radix", &mesh::samp_radix, "sampling: radix pass (phase 0 histogram, phase 1 select)");
+  m.def("samp_find", &mesh::samp_find, "sampling: this rank's candidate token per row");
+  m.def("samp_merge", &mesh::samp_merge, "sampling: merge sampled and greedy tokens");
   m.def("kv_pages_copy", &mesh::kv_pages_copy,
         "gather a session's KV pages (every layer) into a contiguous buffer, or scatter one into pages");
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");

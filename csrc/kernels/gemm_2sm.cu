@@ -47,6 +47,7 @@ struct Params {
   int m_tiles, n_tiles, k_blocks;
   int spin;  // 1: waits poll the barrier; 0: waits sleep inside try_wait between polls
   int* err;
+  unsigned long long* trace;  // optional: cluster 0's first 128 k-steps, %globaltimer stamps
 };
 
 struct Bars {
@@ -75,13 +76,13 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(hint)
       : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster),
-               "r"(bytes)
-               : "memory");
-}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Signal-only remote arrive (orders nothing): the stage release the leader relays to its peer, whose
+// ordering against the MMA's reads the leader already obtained from the MMA commit.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 // D[tmem] (+)= A * B^T over the SM pair (issued by the leader; descriptors address both CTAs' tiles).
 __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -178,11 +179,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          if (rank == 0 && (kb_seq >= STAGES)) mbar_arrive_cluster(mapa_shared(smem_u32(&bars->empty[stage]), 1));
+          if (rank == 0 && (kb_seq >= STAGES)) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&bars->empty[stage]), 1));
+          if (p.trace && cluster == 0 && kb_seq < 128) p.trace[(rank ? 128 : 0) + kb_seq] = globaltimer_ns();
           ++kb_seq;
           const uint32_t full = leader_addr(&bars->full[stage]);
-          // the leader's barrier counts both CTAs' bytes; one arrival (the leader's) per phase
-          if (rank == 0) mbar_arrive_expect_tx_cluster(full, 2 * STAGE_BYTES);
+          // the leader's barrier counts both CTAs' bytes; one arrival (the leader's, on its own
+          // barrier through the CTA-local form) per phase
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
           uint8_t* st = stages + (size_t)stage * STAGE_BYTES;
           tma_load_2d_pair(st, &tmA, full, kb * BK, arow, pol_a);
           tma_load_2d_pair(st + HALF_BYTES, &tmB, full, kb * BK, brow, pol_b);
@@ -204,6 +207,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // -------------------------------- MMA issuer (leader only) --------------------------------
     if (rank == 0) {
       constexpr uint32_t IDESC = make_idesc_bf16(TM, TN);
+      long mma_seq = 0;
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -225,6 +229,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
+          if (p.trace && cluster == 0 && lane == 0 && mma_seq < 128) p.trace[256 + mma_seq] = globaltimer_ns();
+          ++mma_seq;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(stages + (size_t)stage * STAGE_BYTES);
@@ -347,7 +353,8 @@ bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi) {
   return M >= 1 && N >= 1 && K >= 1;
 }
 
-void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err) {
+void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err,
+              const c10::optional<at::Tensor>& trace) {
   using namespace g2sm;
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
               "gemm_2sm: bf16 operands");
@@ -378,6 +385,11 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
     return (e && e[0] == '0') ? 0 : 1;
   }();
   p.spin = spin;
+  p.trace = nullptr;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 384, "gemm_2sm: trace");
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   int sms = 0;
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, A.get_device()));
   const int clusters = std::max(1, std::min(p.m_tiles * p.n_tiles, sms / 2));

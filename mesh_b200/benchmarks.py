@@ -231,6 +231,18 @@ def gemmcmp(args):
         row[f"{name}_tflops"] = round(flops / us / 1e6, 1)
         row[f"{name}_frac"] = round(flops / us / 1e6 / tf, 3)
     ops.scratch(dev).check("gemmcmp")
+    if args.trace:
+        tr = torch.zeros(384, dtype=torch.int64, device=dev)
+        ops.gemm_pair(a, bs[0], out, trace=tr)
+        torch.cuda.synchronize()
+        t = tr.cpu().double()
+        t0 = t[t > 0].min()
+        rel = lambda x: [round(float(v - t0) / 1e3, 2) if v > 0 else None for v in x]
+        row["trace_leader_producer_us"] = rel(t[0:24])
+        row["trace_peer_producer_us"] = rel(t[128:152])
+        row["trace_mma_full_us"] = rel(t[256:280])
+        d = (t[256 + 64] - t[256]) / 64 / 1e3 if t[256 + 64] > 0 else None
+        row["trace_mma_us_per_kstep"] = round(float(d), 3) if d is not None else None
     print(json.dumps(row), flush=True)
 
 
@@ -546,6 +558,7 @@ def main():
     c8.add_argument("--K", type=int, default=4096)
     c8.add_argument("--iters", type=int, default=20)
     c8.add_argument("--impls", nargs="+", default=["pair", "one_sm", "cublas"])
+    c8.add_argument("--trace", action="store_true")
     c5 = sub.add_parser("allreduce")
     c5.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 4096, 8192])
     c5.add_argument("--hidden", type=int, nargs="+", default=[4096, 8192])

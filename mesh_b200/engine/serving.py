@@ -91,6 +91,8 @@ class DecodeGraphs:
         self.slot = torch.full((max_batch,), -1, dtype=torch.int64, device=dev)
         self.seq_lens = torch.ones(max_batch, dtype=torch.int32, device=dev)
         self.block_tables = torch.zeros(max_batch, max_pages_per_seq, dtype=torch.int32, device=dev)
+        # per-slot sampling parameters (1/T with 0 = greedy, top_p, threshold) of sampled steps
+        self.samp = torch.zeros(3, max_batch, dtype=torch.float32, device=dev)
         self.max_pages = max_pages_per_seq
         self.use_graphs = use_graphs
         self.buckets = [b for b in buckets if b <= max_batch] or [max_batch]
@@ -108,24 +110,30 @@ class DecodeGraphs:
                 return b
         raise ValueError(f"decode batch {n} exceeds max batch {self.max_batch}")
 
-    def meta(self, b: int) -> StepMeta:
-        return StepMeta(ids=self.ids[:b], pos=self.pos[:b], slot=self.slot[:b], block_tables=self.block_tables[:b],
-                        seq_lens=self.seq_lens[:b], max_q_len=self.max_pages * self.runner.kv.page_size,
-                        decode=True)
+    def meta(self, b: int, mode: int = 0) -> StepMeta:
+        """mode 0 greedy, 1 sampled (vocabulary-order CDF rows only), 2 sampled with top-p rows."""
+        m = StepMeta(ids=self.ids[:b], pos=self.pos[:b], slot=self.slot[:b], block_tables=self.block_tables[:b],
+                     seq_lens=self.seq_lens[:b], max_q_len=self.max_pages * self.runner.kv.page_size,
+                     decode=True)
+        if mode:
+            m.inv_t, m.top_p, m.thr, m.nucleus = self.samp[0, :b], self.samp[1, :b], self.samp[2, :b], mode == 2
+        return m
 
-    def _run(self, b: int):
-        out = self.runner.forward(self.meta(b), self.bufs.setdefault(b, {}))
+    def _run(self, key):
+        b, mode = key if isinstance(key, tuple) else (key, 0)
+        out = self.runner.forward(self.meta(b, mode), self.bufs.setdefault(key, {}))
         # next ids overwrite the input ids in place (embedding already consumed them)
         self.ids[:b].copy_(out)
         return out
 
-    def capture(self, b: int):
-        if b in self.graphs or not self.use_graphs:
+    def capture(self, key):
+        if key in self.graphs or not self.use_graphs:
             return
+        b = key[0] if isinstance(key, tuple) else key
         # warm-up outside capture sizes the workspaces and sets kernel attributes
         saved = (self.ids.clone(), self.pos.clone(), self.slot.clone(), self.seq_lens.clone())
         self.slot[:b].fill_(-1)
-        self._run(b)
+        self._run(key)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
@@ -134,24 +142,25 @@ class DecodeGraphs:
         n0 = ops.LAUNCHES[0]
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, pool=self.pool):
-                self._run(b)
-        self.graph_launches[b] = ops.LAUNCHES[0] - n0
+                self._run(key)
+        self.graph_launches[key] = ops.LAUNCHES[0] - n0
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         if self.pool is None:
             self.pool = g.pool()
-        self.graphs[b] = g
+        self.graphs[key] = g
         self.ids.copy_(saved[0]); self.pos.copy_(saved[1]); self.slot.copy_(saved[2]); self.seq_lens.copy_(saved[3])
 
-    def step(self, b: int):
+    def step(self, b: int, mode: int = 0):
+        key = (b, mode) if mode else b
         if self.use_graphs:
-            if b not in self.graphs:
-                self.capture(b)
-            self.graphs[b].replay()
+            if key not in self.graphs:
+                self.capture(key)
+            self.graphs[key].replay()
             from .. import ops
-            ops._count(self.graph_launches[b])
+            ops._count(self.graph_launches[key])
         else:
-            self._run(b)
+            self._run(key)
 
     def release(self):
         self.graphs.clear()
@@ -197,6 +206,11 @@ class Engine:
                 t = torch.empty(max_batch * 4, dtype=torch.int32).pin_memory()  # pos | seq | slot (int64)
                 self._stage.append((t, torch.cuda.Event()))
         self._stage_i = 0
+        self._fstage = []
+        if self.device.type == "cuda":
+            for _ in range(4):
+                self._fstage.append((torch.empty(max_batch * 3, dtype=torch.float32).pin_memory(), torch.cuda.Event()))
+        self._fstage_i = 0
         self.steps = 0
         self.stats = dict(prefill_tokens=0, decode_tokens=0, decode_steps=0, prefill_chunks=0,
                           peak_batch_size=0)
@@ -295,27 +309,21 @@ class Engine:
                      block_tables=torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True),
                      seq_lens=pin(klen, torch.int32), cu_q=pin(cu, torch.int32), last_idx=pin(last, torch.int64),
                      max_q_len=max(b - a for _, a, b in items), decode=False)
-        sampled = [i for i, (s, a, b) in enumerate(items) if s.temperature > 0.0 and b == len(s.prompt)]
-        r = self.runner
+        sampled = [i for i, (s, a, b) in enumerate(items)
+                   if s.temperature > 0.0 and s.top_p > 0.0 and b == len(s.prompt)]
         if sampled:
-            r.keep_logits = True
-        try:
-            next_ids = r.forward(m)
-        finally:
-            r.keep_logits = False
-        if sampled:
-            import torch.distributed as dist
-            from ..ops.sampling import sample
-            logits = r.last_logits
-            if r.world > 1:
-                parts = [torch.empty_like(logits) for _ in range(r.world)]
-                dist.all_gather(parts, logits.contiguous(), group=r.group)
-                logits = torch.cat(parts, -1)[:, :self.cfg.vocab_size]
-            next_ids = next_ids.clone()
+            # the first token of a sampled session is drawn on the device like the decode steps'
+            from ..oracle.tensor_ops import deterministic_sample_threshold
+            prm = np.zeros((3, len(items)), dtype=np.float32)
             for i in sampled:
                 s_ = items[i][0]
-                next_ids[i] = sample(logits[i:i + 1], s_.temperature, s_.top_p,
-                                     [s_.seed_base ^ len(s_.prompt)]).to(torch.int32)[0]
+                prm[0, i] = 1.0 / s_.temperature
+                prm[1, i] = s_.top_p
+                prm[2, i] = deterministic_sample_threshold(s_.seed_base ^ len(s_.prompt))
+            pd = torch.from_numpy(prm).pin_memory().to(dev, non_blocking=True)
+            m.inv_t, m.top_p, m.thr = pd[0], pd[1], pd[2]
+            m.nucleus = bool((prm[1][sampled] < 1.0).any())
+        next_ids = self.runner.forward(m)
         finished_prompts = []
         rows, slots = [], []
         for i, (s, a, b) in enumerate(items):
@@ -352,10 +360,9 @@ class Engine:
                and (only is None or s.sid in only)]
         if not act:
             return 0
-        if any(s.temperature > 0.0 for s in act):
-            return self._decode_step_sampled(act)
         hi = max(s.slot for s in act) + 1
         b = self.dec.bucket_for(hi)
+        mode = self._stage_sampling(act, b)
         staged = None
         if self._stage and b <= self._stage[0][0].shape[0] // 4:
             staged, ev = self._stage[self._stage_i]
@@ -398,7 +405,7 @@ class Engine:
         if self.bt_dirty:
             d.block_tables.copy_(torch.from_numpy(self.bt_host).pin_memory(), non_blocking=True)
             self.bt_dirty = False
-        d.step(b)
+        d.step(b, mode)
         if partial:
             d.ids[:b].copy_(torch.where(mask, d.ids[:b], keep_ids))
         row = len(self.hist_rows)
@@ -421,55 +428,28 @@ class Engine:
                 self._retire(s)
         return len(act)
 
-    def _decode_step_sampled(self, act) -> int:
-        """Decode step with temperature/top-p sampling: eager forward keeping fp32 logits, gathered
-        across TP ranks, then the reference's seeded device sampler."""
-        import torch.distributed as dist
-        from ..ops.sampling import sample
-        from ..models.llama import StepMeta
-        n = len(act)
-        pos, seq, slot, bt = [], [], [], np.zeros((n, self.max_pages_per_seq), dtype=np.int32)
-        for i, s in enumerate(act):
-            p = s.kv_len
-            self._ensure_pages(s, p + 1)
-            pos.append(p)
-            seq.append(p + 1)
-            slot.append(s.pages[p // self.page_size] * self.page_size + p % self.page_size)
-            bt[i, :len(s.pages)] = s.pages
-        dev = self.device
-        ids = torch.stack([self.dec.ids[s.slot] for s in act])
-        m = StepMeta(ids=ids, pos=torch.tensor(pos, dtype=torch.int32, device=dev),
-                     slot=torch.tensor(slot, dtype=torch.int64, device=dev),
-                     block_tables=torch.from_numpy(bt).to(dev), seq_lens=torch.tensor(seq, dtype=torch.int32, device=dev),
-                     max_q_len=self.max_pages_per_seq * self.page_size, decode=True)
-        r = self.runner
-        r.keep_logits = True
-        try:
-            r.forward(m)
-        finally:
-            r.keep_logits = False
-        logits = r.last_logits
-        if r.world > 1:
-            parts = [torch.empty_like(logits) for _ in range(r.world)]
-            dist.all_gather(parts, logits.contiguous(), group=r.group)
-            logits = torch.cat(parts, -1)[:, :self.cfg.vocab_size]
-        toks = []
-        for i, s in enumerate(act):
-            seed = s.seed_base ^ (s.kv_len + 1)
-            toks.append(sample(logits[i:i + 1], s.temperature, s.top_p, [seed]))
-        toks = torch.cat(toks).to(torch.int32)
-        for i, s in enumerate(act):
-            self.dec.ids[s.slot] = toks[i]
-            s.kv_len += 1
-            s.n_generated += 1
-            s.decode_steps_served += 1
-        self.hist_first.append(([s.sid for s in act], toks))
-        self.stats["decode_tokens"] += n
-        self.stats["decode_steps"] += 1
-        for s in act:
-            if s.done:
-                self._retire(s)
-        return n
+    def _stage_sampling(self, act, b: int) -> int:
+        """Per-slot sampling parameters of this decode step (1/T, top_p, threshold of the seed for the
+        token's position) copied to the device; returns the graph mode (0 greedy, 1 sampled with
+        vocabulary-order rows only, 2 with top-p rows)."""
+        samp = [s for s in act if s.temperature > 0.0 and s.top_p > 0.0]
+        if not samp:
+            return 0
+        from ..oracle.tensor_ops import deterministic_sample_threshold
+        buf, ev = self._fstage[self._fstage_i]
+        self._fstage_i = (self._fstage_i + 1) % len(self._fstage)
+        ev.synchronize()
+        h = buf.numpy()[:3 * b].reshape(3, b)
+        h[:] = 0.0
+        nucleus = False
+        for s in samp:
+            h[0, s.slot] = 1.0 / s.temperature
+            h[1, s.slot] = s.top_p
+            h[2, s.slot] = deterministic_sample_threshold(s.seed_base ^ (s.kv_len + 1))
+            nucleus |= s.top_p < 1.0
+        self.dec.samp[:, :b].copy_(buf[:3 * b].view(3, b), non_blocking=True)
+        ev.record()
+        return 2 if nucleus else 1
 
     # ----------------------------------------------------------------------------- handoff
     def export_session(self, sid: int) -> SessionHandoff:

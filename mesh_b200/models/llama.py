@@ -75,6 +75,11 @@ class StepMeta:
     last_idx: Optional[torch.Tensor] = None  # [S] int64 rows whose logits are needed (prefill)
     max_q_len: int = 1
     decode: bool = True
+    # per-row sampling parameters (fp32 [S]: 1/T with 0 = greedy, top_p, threshold r); None = greedy
+    inv_t: Optional[torch.Tensor] = None
+    top_p: Optional[torch.Tensor] = None
+    thr: Optional[torch.Tensor] = None
+    nucleus: bool = True   # some row has 0 < top_p < 1 (the sampler's radix passes are needed)
 
 
 class LlamaRunner:
@@ -112,6 +117,7 @@ class LlamaRunner:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
         self._cand_gather = None
+        self._sampler = None
         # keep fp32 logits (tests, sampling); the greedy decode path fuses argmax into the LM head
         self.keep_logits = False
         self.last_logits = None
@@ -235,7 +241,8 @@ class LlamaRunner:
         else:
             final, S = normed, T
         cand = buf("cand", (S, 2), torch.float32)
-        if self.keep_logits or S > ops.SWAP_AB_MAX_TOKENS:
+        sampled = m.inv_t is not None
+        if self.keep_logits or sampled or S > ops.SWAP_AB_MAX_TOKENS:
             logits = buf("logits", (S, w.vocab_local), torch.float32)
             ops.linear(final, w.lm_head, out=logits, epi=ops.EPI_STORE_F32)
             ops.argmax_partial(logits, w.vocab_start, cand)
@@ -244,11 +251,23 @@ class LlamaRunner:
             tiles = buf("cand_tiles", ((w.vocab_local + 127) // 128, S, 2), torch.float32)
             ops.lm_head_argmax(final, w.lm_head, w.vocab_start, tiles, cand)
         ids_out = buf("next_ids", (S,), torch.int32)
+        greedy = buf("greedy_ids", (S,), torch.int32) if sampled else ids_out
         if self.world == 1:
-            ops.argmax_merge(cand.view(1, S, 2), ids_out)
+            ops.argmax_merge(cand.view(1, S, 2), greedy)
         else:
             gathered = buf("cand_all", (self.world, S, 2), torch.float32)
             dist.all_gather_into_tensor(gathered.view(-1), cand.view(-1), group=self.group)
-            ops.argmax_merge(gathered, ids_out)
+            ops.argmax_merge(gathered, greedy)
+        if sampled:
+            # temperature / top-p rows on the device over this rank's vocabulary slice
+            self.sampler(S).sample(logits, m.inv_t, m.top_p, m.thr, greedy, w.vocab_start, ids_out,
+                                   nucleus=m.nucleus)
         rng(None)
         return ids_out
+
+    def sampler(self, rows: int):
+        """The device sampler of this runner (buffers for at least ``rows`` rows)."""
+        from ..ops.sampling import DeviceSampler
+        if self._sampler is None or self._sampler.B < rows:
+            self._sampler = DeviceSampler(max(rows, 64), self.device, self.group, self.world, self.rank)
+        return self._sampler

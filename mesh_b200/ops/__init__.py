@@ -178,9 +178,12 @@ PAIR_GEMM_MIN_TOKENS = 512
 _PAIR_GEMM = os.environ.get("MESH_PAIR_GEMM", "0") == "1"
 
 
-def gemm_pair(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16) -> torch.Tensor:
-    """out = x @ w.T (EPI_SILU_BF16: SiLU(gate) * up of the interleaved gate/up product) on SM pairs."""
-    ext().gemm_2sm(x, w, out, epi, scratch(x.device).err)
+def gemm_pair(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EPI_STORE_BF16,
+              trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = x @ w.T (EPI_SILU_BF16: SiLU(gate) * up of the interleaved gate/up product) on SM pairs.
+    trace: optional int64 [384] of %globaltimer stamps for the first pair (producer empty-waits of both
+    CTAs, then the MMA thread's full-waits)."""
+    ext().gemm_2sm(x, w, out, epi, scratch(x.device).err, trace)
     _count()
     return out
 

@@ -26,6 +26,7 @@ ext_modules = [
             "csrc/kernels/attn_prefill_tc.cu",
             "csrc/kernels/kv_pages.cu",
             "csrc/kernels/gemm_2sm.cu",
+            "csrc/kernels/sampling.cu",
             "csrc/kernels/allreduce.cu",
         ],
         include_dirs=[os.path.join(ROOT, "csrc", "include")],
