@@ -31,7 +31,7 @@ BASELINE_METRIC = "decode tokens/s + p50 TTFT, Llama-3 8B/70B TP at 1/2/4/8 B200
 # The reference publishes no throughput figure. The comparison number per GPU count is the plain
 # PyTorch arm (``--impl torch``: cuBLAS linears, SDPA over gathered pages, NCCL all-reduce) measured
 # with this script on the same B200 pool; None where it has not been measured.
-BASELINE_VALUE = {}
+BASELINE_VALUE = {1: 4052.9, 2: 5900.8}
 
 
 def parse():
@@ -50,9 +50,10 @@ def parse():
     ap.add_argument("--no-nvls", action="store_true",
                     help="keep the fused all-reduce on plain peer loads (no NVSwitch multimem) at every TP degree")
     ap.add_argument("--ar-impl", default="auto",
-                    choices=["auto", "unfused", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
-                    help="TP all-reduce: auto (decode: fused into the o_proj/down GEMM launch), unfused (separate "
-                         "peer-memory kernel), pull one/two-shot, GEMM->reduce-scatter push, or NCCL")
+                    choices=["auto", "unfused", "gemm_ar", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
+                    help="TP all-reduce: auto/unfused (separate peer-memory kernel fused with residual + RMSNorm), "
+                         "gemm_ar (decode: inside the o_proj/down GEMM launch), pull one/two-shot, "
+                         "GEMM->reduce-scatter push, or NCCL")
     return ap.parse_args()
 
 

@@ -144,9 +144,10 @@ class EngineConfig:
     decode_batch_buckets: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
     prefill_chunk_tokens: int = 16384
     use_fused_allreduce: bool = True
-    # auto: decode steps fuse the all-reduce into the o_proj/down GEMM launch, prefill uses the
-    # separate one-shot/two-shot kernel; unfused: the separate kernel for decode too;
-    # oneshot | twoshot | push | push_oneshot | nccl: that all-reduce everywhere
+    # auto: the separate peer-memory all-reduce + residual + RMSNorm kernel after the o_proj / down
+    # GEMM, one-shot or two-shot by size (unfused: the same); gemm_ar: decode steps run the
+    # all-reduce inside the GEMM's launch; oneshot | twoshot | push | push_oneshot | nccl: that
+    # all-reduce everywhere
     allreduce_impl: str = "auto"
     # allow the fused all-reduce to use NVSwitch NVLS (multimem loads/stores) when the node has it;
     # it is used from 8 ranks up, where it measured faster (TP8 decode 23.98k vs 22.74k tok/s),

@@ -8,7 +8,7 @@ Per layer (reference ``forward_layer``, ``agent/src/inference/forward_pass.rs:19
     attn  = paged GQA attention                           (decode: split-KV; prefill: flash)
     part  = tcgen05 GEMM(attn, wo)                        -> own slot of the symmetric workspace
     resid, normed = AR(part) + resid, RMSNorm(mlp_norm)   (ar_fused_norm over NVLink; TP=1: add_rmsnorm;
-                                                          decode TP>1: one launch, gemm_allreduce_norm)
+                                                          opt-in at decode: one launch, gemm_allreduce_norm)
     h     = tcgen05 GEMM(normed, wgu) with SiLU(gate)*up epilogue
     part  = tcgen05 GEMM(h, wdown)
     resid, normed = AR(part) + resid, RMSNorm(next attn_norm or final_norm)
@@ -108,11 +108,12 @@ class LlamaRunner:
         # "push": the o_proj / down GEMM epilogues scatter partial rows to their owner ranks over
         # NVLink (fused GEMM -> reduce-scatter); otherwise GEMMs write locally and the AR kernel pulls
         self.push_rs = self.use_fused_ar and ecfg.allreduce_impl in ("push", "push_oneshot")
-        # decode-sized steps run o_proj / down_proj with the all-reduce, residual add and RMSNorm in
-        # the GEMM's own launch ("auto"); MESH_GEMM_AR=0 or an explicit all-reduce choice keeps the
-        # separate all-reduce kernel
-        self.gemm_ar = (self.use_fused_ar and ecfg.allreduce_impl == "auto" and self.H % 8 == 0 and
-                        self.H <= 8192 and os.environ.get("MESH_GEMM_AR", "1") != "0")
+        # "gemm_ar": decode-sized steps run o_proj / down_proj with the all-reduce, residual add and
+        # RMSNorm in the GEMM's own launch. Measured at TP2 it is slower than the GEMM followed by
+        # the separate fused all-reduce kernel (decode step 3.93 vs 3.42 ms), so "auto" keeps the
+        # separate kernel and the one-launch form is opt-in.
+        self.gemm_ar = (self.use_fused_ar and ecfg.allreduce_impl == "gemm_ar" and self.H % 8 == 0 and
+                        self.H <= 8192)
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)

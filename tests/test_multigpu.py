@@ -230,11 +230,11 @@ def _timeout_check(rank, world):
     assert torch.allclose(ws.resid(8).float(), torch.full((8, H), float(world), device=dev))
 
 
-def _tp_logits(rank, world, preset="small", layers=0, nvls=False):
-    """Prefill of one prompt, then decode steps of a 3-session batch (the decode steps take the
-    fused GEMM + all-reduce path at TP>1), teacher-forced with the TP=1 run's greedy tokens: every
-    step's full-vocabulary logits at TP=world against TP=1, and each TP=world token equal to the
-    argmax of its own logits."""
+def _tp_logits(rank, world, preset="small", layers=0, nvls=False, ar="auto"):
+    """Prefill of one prompt, then decode steps of a 3-session batch (with ar="gemm_ar" the decode
+    steps run the all-reduce inside the GEMM launch), teacher-forced with the TP=1 run's greedy
+    tokens: every step's full-vocabulary logits at TP=world against TP=1, and each TP=world token
+    equal to the argmax of its own logits."""
     import torch.distributed as dist
     from mesh_b200.config import EngineConfig, get_preset
     from mesh_b200.models.llama import KVPool, LlamaRunner, StepMeta
@@ -246,7 +246,7 @@ def _tp_logits(rank, world, preset="small", layers=0, nvls=False):
         cfg = cfg.replace(num_layers=layers)
     if cfg.num_kv_heads % world:
         return f"{preset} has {cfg.num_kv_heads} KV heads, not divisible over {world} ranks"
-    ecfg = EngineConfig(max_seq_len=256, nvls=nvls)
+    ecfg = EngineConfig(max_seq_len=256, nvls=nvls, allreduce_impl=ar)
     gen = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (40, 17, 33)]
     steps = 4
@@ -340,13 +340,14 @@ def test_allreduce_bounded_wait_reports_timeout_2gpu():
     _run(_timeout_check, 2)
 
 
-def test_tp2_logits_match_tp1():
+@pytest.mark.parametrize("ar", ["auto", "gemm_ar"])
+def test_tp2_logits_match_tp1(ar):
     _need(2)
-    _run(_tp_logits, 2)
+    _run(_tp_logits, 2, "small", 0, False, ar)
 
 
 @pytest.mark.parametrize("world", [4, 8])
 def test_tpn_llama3_shape_logits_match_tp1(world):
     """Llama-3-8B-shaped (2 layers) at TP=4/8, NVLS on at 8 ranks as in serving."""
     _need(world)
-    _run(_tp_logits, world, "llama3-8b", 2, world >= 8)
+    _run(_tp_logits, world, "llama3-8b", 2, world >= 8, "gemm_ar")
