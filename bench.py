@@ -31,7 +31,7 @@ BASELINE_METRIC = "decode tokens/s + p50 TTFT, Llama-3 8B/70B TP at 1/2/4/8 B200
 # The reference publishes no throughput figure. The comparison number per GPU count is the plain
 # PyTorch arm (``--impl torch``: cuBLAS linears, SDPA over gathered pages, NCCL all-reduce) measured
 # with this script on the same B200 pool; None where it has not been measured.
-BASELINE_VALUE = {1: 4052.9, 2: 5900.8}
+BASELINE_VALUE = {1: 4052.9, 2: 5900.8, 4: 7732.2}
 
 
 def parse():

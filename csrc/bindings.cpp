@@ -50,6 +50,8 @@ void samp_find(const at::Tensor& logits, const at::Tensor& inv_t, const at::Tens
                const at::Tensor& thr, at::Tensor& st, at::Tensor& active, int64_t vocab_offset, at::Tensor& cand);
 void samp_merge(const at::Tensor& inv_t, const at::Tensor& top_p, const at::Tensor& cand, const at::Tensor& greedy,
                 at::Tensor& ids);
+void embed_peer_norm(const at::Tensor& bases, const at::Tensor& ids, int64_t V, const at::Tensor& gamma, double eps,
+                     at::Tensor& resid, at::Tensor& normed, at::Tensor& err);
 void kv_pages_copy(at::Tensor& k_pool, at::Tensor& v_pool, at::Tensor& buf, const at::Tensor& pages, bool to_buf);
 void ar_fused_norm(const at::Tensor& bases, int64_t off_flags, int64_t off_p0, int64_t off_p1, int64_t off_resid,
                    int64_t off_normed, int64_t rank, int64_t world, int64_t T, int64_t H, int64_t parity,
@@ -98,6 +100,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("samp_radix", &mesh::samp_radix, "sampling: radix pass (phase 0 histogram, phase 1 select)");
   m.def("samp_find", &mesh::samp_find, "sampling: this rank's candidate token per row");
   m.def("samp_merge", &mesh::samp_merge, "sampling: merge sampled and greedy tokens");
+  m.def("embed_peer_norm", &mesh::embed_peer_norm,
+        "vocabulary-parallel embedding read from the owner rank's table over NVLink, fused with RMSNorm");
   m.def("kv_pages_copy", &mesh::kv_pages_copy,
         "gather a session's KV pages (every layer) into a contiguous buffer, or scatter one into pages");
   m.def("ar_fused_norm", &mesh::ar_fused_norm, "peer-memory all-reduce + residual + RMSNorm");

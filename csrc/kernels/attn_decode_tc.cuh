@@ -293,10 +293,10 @@ inline void launch_attn_decode_tc_g(const CUtensorMap& tk, const CUtensorMap& tv
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_decode_tc_smem());
     configured[dev] = true;
   }
-  launch_k(kern, dim3(B, a.hkv, a.splits), dim3(160), attn_decode_tc_smem(), st, tk, tv, a);
+  C10_CUDA_CHECK(launch_k(kern, dim3(B, a.hkv, a.splits), dim3(160), attn_decode_tc_smem(), st, tk, tv, a));
   if (a.splits > 1)
-    launch_k(attn_decode_combine_kernel<128>, dim3(B, a.hkv * G), dim3(128), 0, st, (const float*)a.ws, a.out,
-             a.hkv * G, a.splits);
+    C10_CUDA_CHECK(launch_k(attn_decode_combine_kernel<128>, dim3(B, a.hkv * G), dim3(128), 0, st,
+                            (const float*)a.ws, a.out, a.hkv * G, a.splits));
 }
 
 }  // namespace mesh

@@ -403,3 +403,114 @@ void argmax_merge(const at::Tensor& cand, at::Tensor& ids) {
 }
 
 }  // namespace mesh
+
+namespace mesh {
+
+// Vocabulary-parallel embedding fused with the first RMSNorm: rank r holds rows [start_r, start_r +
+// n_r) of the table (near-equal contiguous ranges, larger first) in a symmetric allocation that
+// every peer maps; each token's row is read from its owner's table (NVLink peer loads, or local),
+// written to `resid` and normalised into `normed`. The tables are written once at load and only
+// read afterwards, so no synchronisation between ranks is needed. One CTA per token.
+struct EmbedPeerArgs {
+  unsigned long long base[8];  // table base of each rank as mapped here
+  const int* ids;
+  int V, H, world;
+  const __nv_bfloat16* gamma;
+  float eps;
+  __nv_bfloat16* resid;
+  __nv_bfloat16* normed;
+  int* err;
+};
+
+__global__ void __launch_bounds__(256) embed_peer_norm_kernel(const EmbedPeerArgs a) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  griddep_wait();
+  griddep_launch_dependents();
+  int id = a.ids[t];
+  const bool bad = id < 0 || id >= a.V;
+  if (bad) {
+    if (threadIdx.x == 0) record_error(a.err, ERR_BAD_ARGUMENT);
+    id = 0;
+  }
+  const int base = a.V / a.world, extra = a.V % a.world;
+  const int big = extra * (base + 1);
+  const int r = id < big ? id / (base + 1) : extra + (id - big) / base;
+  const int row = id - (id < big ? r * (base + 1) : big + (r - extra) * base);
+  const uint4* src = reinterpret_cast<const uint4*>(a.base[r]) + (long)row * (a.H / 8);
+  uint4* res = reinterpret_cast<uint4*>(a.resid + (long)t * a.H);
+  const int nvec = a.H / 8;
+  uint4 v[4];  // H <= 8192: at most 4 chunks of 16 bytes per thread
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    if (c < nvec) {
+      v[j] = bad ? make_uint4(0, 0, 0, 0) : src[c];
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x0, x1;
+        unpack_bf16x2(u[q], x0, x1);
+        ss += x0 * x0 + x1 * x1;
+      }
+      res[c] = v[j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / (float)a.H + a.eps);
+  uint4* nrm = reinterpret_cast<uint4*>(a.normed + (long)t * a.H);
+  const uint4* g = reinterpret_cast<const uint4*>(a.gamma);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    if (c < nvec) {
+      const uint4 gv = g[c];
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[j]);
+      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&gv);
+      uint4 o;
+      uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x0, x1, g0, g1;
+        unpack_bf16x2(u[q], x0, x1);
+        unpack_bf16x2(gu[q], g0, g1);
+        ou[q] = pack_bf16x2(x0 * inv * g0, x1 * inv * g1);
+      }
+      nrm[c] = o;
+    }
+  }
+}
+
+void embed_peer_norm(const at::Tensor& bases, const at::Tensor& ids, int64_t V, const at::Tensor& gamma, double eps,
+                     at::Tensor& resid, at::Tensor& normed, at::Tensor& err) {
+  TORCH_CHECK(bases.device().is_cpu() && bases.scalar_type() == at::kLong && bases.numel() >= 1 && bases.numel() <= 8,
+              "embed_peer_norm: CPU int64 table bases of 1..8 ranks");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_cuda(), "embed_peer_norm: int32 ids");
+  const int T = ids.numel(), H = gamma.numel();
+  TORCH_CHECK(H % 8 == 0 && H <= 8192 && resid.size(0) >= T && normed.size(0) >= T && resid.size(1) == H &&
+                  resid.is_contiguous() && normed.is_contiguous(),
+              "embed_peer_norm: H % 8 == 0, H <= 8192, resid/normed [T, H]");
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(ids.device());
+  EmbedPeerArgs a{};
+  a.world = bases.numel();
+  for (int i = 0; i < a.world; ++i) a.base[i] = (unsigned long long)bases.data_ptr<int64_t>()[i];
+  a.ids = ids.data_ptr<int>();
+  a.V = (int)V;
+  a.H = H;
+  a.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr());
+  a.eps = (float)eps;
+  a.resid = reinterpret_cast<__nv_bfloat16*>(resid.data_ptr());
+  a.normed = reinterpret_cast<__nv_bfloat16*>(normed.data_ptr());
+  a.err = err.data_ptr<int>();
+  C10_CUDA_CHECK(launch_k(embed_peer_norm_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(), a));
+}
+
+}  // namespace mesh

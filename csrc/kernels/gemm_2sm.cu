@@ -34,7 +34,7 @@ constexpr int TN = 256;                        // output columns per SM pair
 constexpr int BK = 64;                         // k elements per stage (one 128-byte swizzle atom)
 constexpr uint32_t HALF_BYTES = 128 * BK * 2;  // 128 rows x 64 bf16: one CTA's A (or B) stage
 constexpr uint32_t STAGE_BYTES = 2 * HALF_BYTES;
-constexpr int STAGES = 6;
+constexpr int MAX_STAGES = 7;                  // shared memory holds at most 7 stages of 32 KB
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;            // two 256-column accumulators
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
@@ -46,13 +46,14 @@ struct Params {
   int ldo;            // out row stride (elements)
   int m_tiles, n_tiles, k_blocks;
   int spin;  // 1: waits poll the barrier; 0: waits sleep inside try_wait between polls
+  int stages;
   int* err;
   unsigned long long* trace;  // optional: cluster 0's first 128 k-steps, %globaltimer stamps
 };
 
 struct Bars {
-  uint64_t full[STAGES];   // leader: both CTAs' loads of the stage landed
-  uint64_t empty[STAGES];  // each CTA: the stage's MMAs are done with its shared memory (leader:
+  uint64_t full[MAX_STAGES];   // leader: both CTAs' loads of the stage landed
+  uint64_t empty[MAX_STAGES];  // each CTA: the stage's MMAs are done with its shared memory (leader:
                            // MMA commit; peer: relayed by the leader's producer)
   uint64_t tfull[2];       // each CTA: accumulator complete (peer: relayed by the leader's epilogue)
   uint64_t tempty[2];      // leader: both CTAs' epilogues finished reading the accumulator
@@ -62,7 +63,7 @@ struct Bars {
   int epi_ok;
 };
 
-constexpr size_t smem_bytes() { return 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Bars); }
+constexpr size_t smem_bytes(int stages) { return 1024 + (size_t)stages * STAGE_BYTES + sizeof(Bars); }
 
 __device__ __forceinline__ uint32_t leader_addr(const void* p) { return mapa_shared(smem_u32(p), 0); }
 
@@ -122,14 +123,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* stages = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  Bars* bars = reinterpret_cast<Bars*>(stages + (size_t)STAGES * STAGE_BYTES);
+  Bars* bars = reinterpret_cast<Bars*>(stages + (size_t)p.stages * STAGE_BYTES);
+  const int STAGES = p.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader of the pair
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const int tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < MAX_STAGES; ++i) {
       mbar_init(&bars->full[i], 1);
       mbar_init(&bars->empty[i], 1);
     }
@@ -393,7 +395,13 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
   int sms = 0;
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, A.get_device()));
   const int clusters = std::max(1, std::min(p.m_tiles * p.n_tiles, sms / 2));
-  const size_t smem = smem_bytes();
+  static const int stages = [] {
+    const char* e = std::getenv("MESH_PAIR_STAGES");
+    const int v = e ? std::atoi(e) : 6;
+    return std::max(2, std::min(v, MAX_STAGES));
+  }();
+  p.stages = stages;
+  const size_t smem = smem_bytes(stages);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto go = [&](auto kern) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

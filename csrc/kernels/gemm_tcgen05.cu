@@ -1643,7 +1643,7 @@ static void launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const Gem
                          cudaStream_t stream) {
   auto kern = gemm_tcgen05_kernel<EPI, TRANS>;
   configure_kernel<EPI, TRANS>();
-  launch_kc(kern, dim3(grid), dim3(NUM_THREADS), smem, stream, p.ck > 1 ? p.ck : 1, ta, tb, p);
+  C10_CUDA_CHECK(launch_kc(kern, dim3(grid), dim3(NUM_THREADS), smem, stream, p.ck > 1 ? p.ck : 1, ta, tb, p));
 }
 
 // Largest number of co-resident clusters of `C` CTAs of this kernel (every CTA of a cluster split

@@ -134,7 +134,14 @@ class TorchTPRunner:
         if T > self.max_tokens:
             raise ValueError(f"step of {T} tokens exceeds runner capacity {self.max_tokens}")
         H, eps, D = self.H, c.rms_norm_eps, self.D
-        resid = F.embedding(m.ids.long(), w.embedding)
+        if self.world == 1:
+            resid = F.embedding(m.ids.long(), w.embedding)
+        else:
+            # vocabulary-parallel embedding: rows this rank holds, zeros elsewhere, summed over ranks
+            local = m.ids.long() - w.vocab_start
+            hit = (local >= 0) & (local < w.vocab_local)
+            resid = F.embedding(local.clamp(0, w.vocab_local - 1), w.embedding) * hit[:, None].to(w.embedding.dtype)
+            dist.all_reduce(resid, group=self.group)
         normed = F.rms_norm(resid, (H,), w.layers[0].attn_norm, eps)
         pos = m.pos.long()
         cos, sin = self.cos[pos], self.sin[pos]

@@ -57,6 +57,21 @@ class Session:
         return self.n_generated >= self.max_new_tokens
 
 
+def _on_device(fn):
+    """Run an Engine method with the engine's GPU as the current device: its CUDA events, capture
+    stream and staging-ring fences then belong to that GPU even when the process's current device
+    is another one (several engines in one process)."""
+    import functools
+
+    @functools.wraps(fn)
+    def wrapped(self, *a, **k):
+        if self.device.type != "cuda":
+            return fn(self, *a, **k)
+        with torch.cuda.device(self.device):
+            return fn(self, *a, **k)
+    return wrapped
+
+
 @dataclass
 class SessionHandoff:
     """A decoding session lifted out of one engine: its request, the tokens so far and its KV pages
@@ -261,6 +276,7 @@ class Engine:
     def _free_slots(self) -> List[int]:
         return [i for i, s in enumerate(self.running) if s is None]
 
+    @_on_device
     def prefill_step(self, token_budget: Optional[int] = None) -> List[Session]:
         """Prefill a chunk of waiting prompts (whole prompts or the next piece of a long one)."""
         budget = token_budget or self.ecfg.prefill_chunk_tokens
@@ -353,6 +369,7 @@ class Engine:
         return finished_prompts
 
     # ----------------------------------------------------------------------------- decode
+    @_on_device
     def decode_step(self, only=None) -> int:
         """One decode step over the sessions in the decode phase (all of them, or the ``only``
         subset chosen by a microbatch planner); returns the batch size."""
@@ -452,6 +469,7 @@ class Engine:
         return 2 if nucleus else 1
 
     # ----------------------------------------------------------------------------- handoff
+    @_on_device
     def export_session(self, sid: int) -> SessionHandoff:
         """Take a decoding session out of this engine (reference: moving a session between decode
         queues with its KV, coordinator.rs:1916-1957). The generated tokens are read back first; the
@@ -471,6 +489,7 @@ class Engine:
         del self.sessions[sid]
         return h
 
+    @_on_device
     def import_session(self, h: SessionHandoff) -> int:
         """Continue a session exported by ``export_session`` (from this or another engine with the
         same model shard geometry); returns its id here."""
@@ -509,6 +528,7 @@ class Engine:
         self._free_session(s)
 
     # ----------------------------------------------------------------------------- outputs
+    @_on_device
     def flush_history(self):
         """Copy generated tokens to the host (one D2H copy) and append them to sessions."""
         for sids, toks in self.hist_first:
@@ -531,15 +551,18 @@ class Engine:
         else:
             self.decode_step()
 
+    @_on_device
     def run(self):
         while self.has_work():
             self.step()
         self.flush_history()
 
+    @_on_device
     def generate(self, prompts: List[List[int]], max_new_tokens: int) -> List[List[int]]:
         sids = [self.submit(p, max_new_tokens) for p in prompts]
         self.run()
         return [self.sessions[s].generated[:max_new_tokens] for s in sids]
 
+    @_on_device
     def close(self):
         self.dec.release()

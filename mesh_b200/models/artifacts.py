@@ -207,5 +207,5 @@ def shard_to_device_weights(cfg: ModelConfig, tensors: Dict[str, np.ndarray], ra
             wgu=interleave_gate_up(d(tensors[p + "w_gate"].T), d(tensors[p + "w_up"].T), i_pad),
             wdown=d(wd), attn_norm=d(tensors[p + "attn_norm"]), mlp_norm=d(tensors[p + "mlp_norm"])))
     return DeviceWeights(config=cfg, layout=s, vocab_start=v0, vocab_local=vn, i_pad=i_pad,
-                         embedding=d(tensors["embedding"]), final_norm=d(tensors["final_norm"]),
+                         embedding=d(tensors["embedding"][v0:v0 + vn]), final_norm=d(tensors["final_norm"]),
                          lm_head=d(tensors["lm_head"][:, v0:v0 + vn].T), layers=layers)

@@ -117,6 +117,15 @@ class LlamaRunner:
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
+        # vocabulary-parallel embedding: this rank's rows live in a table every peer maps, and each
+        # token's row is read from its owner (one launch, fused with the first RMSNorm)
+        self.emb_table = None
+        if self.world > 1:
+            if weights.embedding.shape[0] != weights.vocab_local:
+                raise ValueError("TP>1 expects this rank's vocabulary rows of the embedding")
+            from ..parallel.symm import SymmTable
+            self.emb_table = SymmTable(weights.embedding, c.vocab_size, group)
+            weights.embedding = self.emb_table.local
         self._cand_gather = None
         self._sampler = None
         # keep fp32 logits (tests, sampling); the greedy decode path fuses argmax into the LM head
@@ -202,8 +211,12 @@ class LlamaRunner:
 
         resid, normed = self._resid_normed(T)
         rng = _nvtx_range
-        ops.embedding(m.ids, w.embedding, resid)
-        ops.add_rmsnorm(resid, w.layers[0].attn_norm, normed, c.rms_norm_eps)
+        if self.emb_table is not None:
+            ops.embed_peer_norm(self.emb_table.bases, m.ids, c.vocab_size, w.layers[0].attn_norm, c.rms_norm_eps,
+                                resid, normed)
+        else:
+            ops.embedding(m.ids, w.embedding, resid)
+            ops.add_rmsnorm(resid, w.layers[0].attn_norm, normed, c.rms_norm_eps)
         qkv_w = (self.hq + 2 * self.hkv) * self.D
         qkv = buf("qkv", (T, qkv_w))
         q = buf("q", (T, self.hq * self.D))

@@ -11,7 +11,8 @@ Reference layout (``[in, out]`` fp32, what the artifact files hold) is produced 
             SiLU·up epilogue stays inside the tile; I_pad rounds the local width up to 64 with zeros
 * ``wdown`` [H, I_pad]
 * ``lm_head`` [V_local, H]  vocab-parallel rows (the reference replicates the full head)
-* ``embedding`` [V, H] replicated; norms [H].
+* ``embedding`` [V, H] at TP=1; at TP>1 only this rank's vocabulary rows [vocab_start, +vocab_local)
+  (the same split as the LM head; other ranks' rows are read over NVLink); norms [H].
 """
 from __future__ import annotations
 
@@ -134,7 +135,7 @@ def device_weights_from_reference(w, rank: int, world: int, device="cpu", dtype=
             attn_norm=t(L["attn_norm"]), mlp_norm=t(L["mlp_norm"]),
         ))
     return DeviceWeights(config=cfg, layout=s, vocab_start=v0, vocab_local=vn, i_pad=i_pad,
-                         embedding=t(w.embedding), final_norm=t(w.final_norm),
+                         embedding=t(w.embedding[v0:v0 + vn]), final_norm=t(w.final_norm),
                          lm_head=t(w.lm_head[:, v0:v0 + vn].T), layers=layers)
 
 
@@ -183,7 +184,7 @@ def synthetic_device_weights(cfg: ModelConfig, rank: int, world: int, seed: int 
             wd = torch.cat([wd, torch.zeros(H, i_pad - s.mlp_cols, device=dev, dtype=dtype)], 1)
         layers.append(LayerDeviceWeights(wqkv=wqkv, wo=wo, wgu=wgu, wdown=wd.contiguous(),
                                          attn_norm=norm("attn_norm", li), mlp_norm=norm("mlp_norm", li)))
-    emb = full("embedding", V, H).to(dtype)
+    emb = full("embedding", V, H)[v0:v0 + vn].to(dtype).contiguous()  # vocabulary-parallel (all rows at TP=1)
     head = full("lm_head", V, H)[v0:v0 + vn].to(dtype).contiguous()
     return DeviceWeights(config=cfg, layout=s, vocab_start=v0, vocab_local=vn, i_pad=i_pad,
                          embedding=emb, final_norm=norm("final_norm"), lm_head=head, layers=layers)

@@ -286,6 +286,14 @@ def attn_prefill(q, kcache, vcache, cu_q, k_lens, block_tables, out, max_q_len: 
     return out
 
 
+def embed_peer_norm(bases: torch.Tensor, ids: torch.Tensor, vocab: int, gamma: torch.Tensor, eps: float,
+                    resid: torch.Tensor, normed: torch.Tensor):
+    """resid = embedding rows of ``ids`` read from the rank that owns each row (``bases``: the
+    symmetric table of every rank), normed = RMSNorm(resid) * gamma. One launch."""
+    ext().embed_peer_norm(bases, ids, vocab, gamma, eps, resid, normed, scratch(ids.device).err)
+    _count()
+
+
 def kv_pages_gather(k_pool: torch.Tensor, v_pool: torch.Tensor, pages, out: Optional[torch.Tensor] = None):
     """[layers, pages, hkv, ps, D] pools -> buffer [2, layers, len(pages), hkv*ps*D] (K then V)."""
     L, P = k_pool.shape[0], k_pool.shape[1]

@@ -199,3 +199,31 @@ class SymmWorkspace:
         s = ops.scratch(self.device)
         ops.ext().ar_barrier(self.bases, self.layout.off_flags, self.rank, self.world, self.epoch, s.err,
                              timeout_s, self.epoch)
+
+
+class SymmTable:
+    """A read-only table sharded by rows over the TP group and mapped into every peer: rank r holds
+    rows [start_r, start_r + n_r) (near-equal contiguous ranges, larger first) of a [rows, cols]
+    bf16 table; ``bases`` lists every rank's allocation as mapped here, so a kernel can read any row
+    from its owner over NVLink. Used for the vocabulary-parallel embedding (each rank keeps 1/TP of
+    the table instead of all of it)."""
+
+    def __init__(self, local: torch.Tensor, total_rows: int, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        rows_max = -(-total_rows // self.world)
+        cols = local.shape[1]
+        # every rank allocates the same size (the largest shard)
+        self.buf = symm_mem.empty(rows_max * cols, dtype=torch.bfloat16, device=local.device)
+        self.buf[: local.numel()].copy_(local.reshape(-1))
+        torch.cuda.synchronize(local.device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group.group_name)
+        ptrs = list(self.handle.buffer_ptrs)
+        if ptrs[self.rank] != self.buf.data_ptr():
+            raise RuntimeError("symmetric table is not at the start of its allocation")
+        self.bases = torch.tensor(ptrs, dtype=torch.int64)
+        self.local = self.buf[: local.numel()].view(local.shape)
+        dist.barrier(self.group)
+

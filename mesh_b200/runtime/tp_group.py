@@ -162,7 +162,8 @@ def build_rank_backend(spec: GroupSpec, rank: int, group=None):
     return GpuBackend(Engine(runner, ecfg, max_batch=spec.max_batch)), cfg, ecfg
 
 
-def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, result_path: Optional[str]):
+def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, result_path: Optional[str],
+               spmd: bool = False):
     import torch
     import torch.distributed as dist
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -173,7 +174,13 @@ def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, res
     ctl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=spec.timeout_s))
     try:
         backend, cfg, ecfg = build_rank_backend(spec, rank, group=dist.group.WORLD if spec.world > 1 else None)
-        if rank == 0:
+        if spmd:
+            # every rank runs the leader's program on its own backend (it must be deterministic)
+            out = leader(backend, cfg, ecfg)
+            if rank == 0 and result_path:
+                with open(result_path, "wb") as f:
+                    f.write(cbor2.dumps(out))
+        elif rank == 0:
             tb = TPGroupBackend(backend, ctl, spec.world)
             try:
                 out = leader(tb, cfg, ecfg)
@@ -190,12 +197,14 @@ def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, res
         dist.destroy_process_group()
 
 
-def run_group(spec: GroupSpec, leader: Callable, workdir: str):
+def run_group(spec: GroupSpec, leader: Callable, workdir: str, spmd: bool = False):
     """Start one process per GPU, run ``leader(backend, model_config, engine_config)`` on rank 0 with
-    the group backend, and return its (CBOR-serialisable) result once every rank has exited."""
+    the group backend, and return its (CBOR-serialisable) result once every rank has exited.
+    ``spmd=True`` instead runs ``leader`` on every rank with that rank's own backend (each rank makes
+    the same calls itself, as the benchmark does); a deterministic program gives the same result."""
     import torch.multiprocessing as mp
     init_file = os.path.join(workdir, "tp_group_store")
     result_path = os.path.join(workdir, "tp_group_result.cbor")
-    mp.spawn(_rank_main, args=(spec, init_file, leader, result_path), nprocs=spec.world, join=True)
+    mp.spawn(_rank_main, args=(spec, init_file, leader, result_path, spmd), nprocs=spec.world, join=True)
     with open(result_path, "rb") as f:
         return cbor2.loads(f.read())

