@@ -528,9 +528,19 @@ class Engine:
         self._free_session(s)
 
     # ----------------------------------------------------------------------------- outputs
+    def check_device(self):
+        """Raise if a kernel of this engine recorded an error (a bounded wait that ran out because a
+        peer rank never arrived, a pipeline timeout, a bad argument). The error word is cleared, so
+        the engine can be reset (``runner.symm.reset()`` on every rank) and used again."""
+        from .. import ops
+        ops.scratch(self.device).check("engine step")
+
     @_on_device
     def flush_history(self):
-        """Copy generated tokens to the host (one D2H copy) and append them to sessions."""
+        """Copy generated tokens to the host (one D2H copy) and append them to sessions, after
+        checking that no kernel of the steps being read back recorded an error."""
+        if self.device.type == "cuda":
+            self.check_device()
         for sids, toks in self.hist_first:
             vals = toks.cpu().tolist()
             for sid, t in zip(sids, vals):

@@ -105,6 +105,8 @@ class LlamaRunner:
         self.max_tokens = max_tokens
         self.symm = None
         self.use_fused_ar = self.world > 1 and ecfg.allreduce_impl != "nccl"
+        # bound of every cross-rank wait inside the collective kernels (reference allreduce timeout)
+        self.ar_timeout = float(ecfg.allreduce_timeout_s)
         # "push": the o_proj / down GEMM epilogues scatter partial rows to their owner ranks over
         # NVLink (fused GEMM -> reduce-scatter); otherwise GEMMs write locally and the AR kernel pulls
         self.push_rs = self.use_fused_ar and ecfg.allreduce_impl in ("push", "push_oneshot")
@@ -162,9 +164,9 @@ class LlamaRunner:
         if self.world == 1:
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
         elif self.push_rs:
-            self.symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T))
+            self.symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout)
         elif self.use_fused_ar:
-            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T),
+            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout,
                                            multicast=self.world >= 8)
         else:  # NCCL baseline
             dist.all_reduce(part, group=self.group)
@@ -186,7 +188,7 @@ class LlamaRunner:
         """resid += sum_ranks(x @ wt.T); normed = RMSNorm(resid) * gamma (row-parallel projection)."""
         T = x.shape[0]
         if self.gemm_ar and T <= ops.SWAP_AB_MAX_TOKENS:
-            self.symm.gemm_allreduce_norm(x, wt, parity, gamma, self.cfg.rms_norm_eps,
+            self.symm.gemm_allreduce_norm(x, wt, parity, gamma, self.cfg.rms_norm_eps, timeout_s=self.ar_timeout,
                                           multicast=self.world >= 8)
             return
         part = self._part_buf(T, parity, bufs)

@@ -333,6 +333,55 @@ def test_vocab_parallel_embedding(world):
     _run(_embed_check, world)
 
 
+def _stall_check(rank, world):
+    """Failure detection through the engine: rank 1 stalls on the host between two decode steps for
+    longer than the collectives' bound (0.5 s, NVLS off), rank 0's all-reduce waits run out, and
+    rank 0's engine raises a clean RuntimeError when it reads the step back; after a collective
+    reset of the workspace both engines step again without error."""
+    import time
+    import torch.distributed as dist
+    from mesh_b200.config import EngineConfig, get_preset
+    from mesh_b200.engine.serving import Engine
+    from mesh_b200.models.llama import KVPool, LlamaRunner
+    from mesh_b200.models.weights import synthetic_device_weights
+    dev = torch.device("cuda", rank)
+    cfg = get_preset("small")
+    ecfg = EngineConfig(max_seq_len=256, nvls=False, allreduce_timeout_s=0.5, tp=world)
+    w = synthetic_device_weights(cfg, rank, world, seed=3, device=dev)
+    kv = KVPool(cfg, w.layout.local_kv_heads, 64, 16, dev)
+    eng = Engine(LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD, max_tokens=256), ecfg, max_batch=4)
+    g = torch.Generator().manual_seed(8)
+    for n in (11, 23):
+        eng.submit(torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist(), 12)
+    while eng.waiting:
+        eng.prefill_step()
+    for _ in range(2):
+        eng.decode_step()
+    eng.flush_history()
+    dist.barrier()
+    if rank == 1:
+        time.sleep(1.5)  # between steps: nothing of this rank is in flight
+    eng.decode_step()
+    raised = False
+    try:
+        eng.flush_history()
+    except RuntimeError as e:
+        raised = "peer timeout" in str(e) or "device error code 4" in str(e)
+    flags = torch.tensor([1 if raised else 0], device=dev)
+    dist.all_reduce(flags)
+    if rank == 0:
+        assert raised, "rank 0's bounded waits must have run out and surfaced as an exception"
+    eng.runner.symm.reset()
+    eng.decode_step()
+    eng.flush_history()  # no error after the reset
+    eng.close()
+
+
+def test_engine_surfaces_peer_stall_2gpu():
+    _need(2)
+    _run(_stall_check, 2)
+
+
 def _need(n):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
