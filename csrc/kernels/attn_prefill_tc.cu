@@ -67,7 +67,8 @@ struct Args {
   int max_pages, hkv, hq, n_ctas, nseq;
   float scale_log2;
   int window;
-  int spin;  // 1: waits poll the barrier; 0: waits sleep inside try_wait between polls
+  int spin;     // 1: waits poll the barrier; 0: waits sleep inside try_wait between polls
+  int pv_wait;  // 1: QK_t(j+1) waits for PV_t(j) to complete (P shares S's TMEM columns)
   int* err;
 };
 
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = 0; t < NT && ok; ++t) {
         if (g.nblk[t] == 0) continue;
         // S_t / P_t of the previous item are free once its last PV_t is done
-        if (tcnt[t] > 0 && !wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
+        if (a.pv_wait && tcnt[t] > 0 && !wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
           ok = false;
           break;
         }
@@ -354,8 +355,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           issue_pv(t, s, j == 0);
           ++tcnt[t];
           if (j + 1 < g.nblk[t]) {
-            // S_t(j+1) overwrites the columns P_t(j) is read from: wait until PV_t(j) is done
-            if (!wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
+            // S_t(j+1) overwrites the columns P_t(j) is read from. With pv_wait the thread waits until
+            // PV_t(j) is done; otherwise it relies on the tensor core executing one thread's MMAs in
+            // issue order (PV_t(j) reads its operands before QK_t(j+1), issued after it, writes)
+            if (a.pv_wait && !wait(&bars->o_done[t], (uint32_t)(tcnt[t] - 1) & 1u)) {
               ok = false;
               break;
             }
@@ -563,6 +566,11 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
     return (e && e[0] == '0') ? 0 : 1;
   }();
   a.spin = spin;
+  static const int pv_wait = [] {
+    const char* e = std::getenv("MESH_ATTN_PV_WAIT");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  a.pv_wait = pv_wait;
   // persistent: one CTA per SM walks the work items (tile pair, KV head, sequence)
   int sms = 0;
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device()));
