@@ -38,7 +38,7 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Te
                      double scale, int64_t window, at::Tensor& err);
 bool attn_prefill_tc_supported(int64_t head_dim, int64_t page_size, int64_t group);
 void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err,
-              const c10::optional<at::Tensor>& trace);
+              const c10::optional<at::Tensor>& trace, int64_t tn);
 bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi);
 void samp_stats(const at::Tensor& logits, const at::Tensor& inv_t, const at::Tensor& gmax, at::Tensor& out,
                 int64_t step);
@@ -93,7 +93,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "paged causal varlen GQA prefill attention on tcgen05 (TMEM scores and accumulator, TMA page loads)");
   m.def("attn_prefill_tc_supported", &mesh::attn_prefill_tc_supported, "shapes the tcgen05 prefill attention serves");
   m.def("gemm_2sm", &mesh::gemm_2sm, "prefill GEMM on SM pairs (tcgen05.mma.cta_group::2, 256x256 tiles)",
-        py::arg("A"), py::arg("B"), py::arg("out"), py::arg("epi"), py::arg("err"), py::arg("trace") = py::none());
+        py::arg("A"), py::arg("B"), py::arg("out"), py::arg("epi"), py::arg("err"), py::arg("trace") = py::none(),
+        py::arg("tn") = 0);
   m.def("gemm_2sm_supported", &mesh::gemm_2sm_supported, "shapes the SM-pair GEMM serves");
   m.def("samp_stats", &mesh::samp_stats, "sampling: row max (step 0) / fixed-point mass (step 1)");
   m.def("samp_init", &mesh::samp_init, "sampling: per-row selection set-up");

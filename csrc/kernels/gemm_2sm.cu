@@ -30,13 +30,17 @@ namespace mesh {
 namespace g2sm {
 
 constexpr int TM = 256;                        // output rows per SM pair (128 per CTA)
-constexpr int TN = 256;                        // output columns per SM pair
 constexpr int BK = 64;                         // k elements per stage (one 128-byte swizzle atom)
-constexpr uint32_t HALF_BYTES = 128 * BK * 2;  // 128 rows x 64 bf16: one CTA's A (or B) stage
-constexpr uint32_t STAGE_BYTES = 2 * HALF_BYTES;
-constexpr int MAX_STAGES = 7;                  // shared memory holds at most 7 stages of 32 KB
+constexpr uint32_t A_BYTES = 128 * BK * 2;     // one CTA's 128 rows of A for one stage
+// Tile width TN (256 or 128 output columns per pair): each CTA stages TN/2 rows of B per stage.
+template <int TN>
+struct Tile {
+  static constexpr uint32_t B_BYTES = (TN / 2) * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * TN;  // two accumulators
+};
+constexpr int MAX_STAGES = 9;                  // 24 KB stages (TN = 128) fit 9 times
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;            // two 256-column accumulators
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 enum Epi : int { STORE_BF16 = 0, SILU_BF16 = 2 };
 
@@ -63,7 +67,8 @@ struct Bars {
   int epi_ok;
 };
 
-constexpr size_t smem_bytes(int stages) { return 1024 + (size_t)stages * STAGE_BYTES + sizeof(Bars); }
+template <int TN>
+constexpr size_t smem_bytes(int stages) { return 1024 + (size_t)stages * Tile<TN>::STAGE_BYTES + sizeof(Bars); }
 
 __device__ __forceinline__ uint32_t leader_addr(const void* p) { return mapa_shared(smem_u32(p), 0); }
 
@@ -117,9 +122,11 @@ __device__ __forceinline__ void tile_mn(int t, const Params& p, int& tm, int& tn
   tn = in / gm;
 }
 
-template <int EPI>
+template <int EPI, int TN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr uint32_t STAGE_BYTES = Tile<TN>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = Tile<TN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* stages = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -173,7 +180,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = cluster; t < tiles && ok; t += nclusters) {
         int tm, tn;
         tile_mn(t, p, tm, tn);
-        const int arow = tm * TM + (int)rank * 128, brow = tn * TN + (int)rank * 128;
+        const int arow = tm * TM + (int)rank * 128, brow = tn * TN + (int)rank * (TN / 2);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           // the leader learns from its MMA commit that both CTAs' copies of the stage were consumed
           // and passes that on to the peer's producer (a plain remote arrive)
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
           uint8_t* st = stages + (size_t)stage * STAGE_BYTES;
           tma_load_2d_pair(st, &tmA, full, kb * BK, arow, pol_a);
-          tma_load_2d_pair(st + HALF_BYTES, &tmB, full, kb * BK, brow, pol_b);
+          tma_load_2d_pair(st + A_BYTES, &tmB, full, kb * BK, brow, pol_b);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -236,7 +243,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(stages + (size_t)stage * STAGE_BYTES);
-            const uint64_t ad = make_sdesc_sw128(a_addr), bd = make_sdesc_sw128(a_addr + HALF_BYTES);
+            const uint64_t ad = make_sdesc_sw128(a_addr), bd = make_sdesc_sw128(a_addr + A_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) umma_pair(d, ad + 2 * k, bd + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
             // the stage is free once these MMAs are done (the producer relays it to the peer)
@@ -355,8 +362,17 @@ bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi) {
   return M >= 1 && N >= 1 && K >= 1;
 }
 
+// 128-column tiles are picked automatically only with MESH_PAIR_AUTO_TN=1 (until measured)
+static bool pair_auto_narrow() {
+  static const bool v = [] {
+    const char* e = std::getenv("MESH_PAIR_AUTO_TN");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err,
-              const c10::optional<at::Tensor>& trace) {
+              const c10::optional<at::Tensor>& trace, int64_t tn) {
   using namespace g2sm;
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
               "gemm_2sm: bf16 operands");
@@ -370,8 +386,6 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
               "gemm_2sm: out [M, N'] with 16-byte aligned rows");
   TORCH_CHECK((A.stride(0) * 2) % 16 == 0 && (B.stride(0) * 2) % 16 == 0, "gemm_2sm: 16-byte row pitch");
   const c10::cuda::CUDAGuard guard(A.device());
-  CUtensorMap ta = tma_map_2d_bf16(A.data_ptr(), K, M, A.stride(0), BK, 128);
-  CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, 128);
   Params p;
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.M = M;
@@ -379,7 +393,27 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
   p.K = K;
   p.ldo = out.stride(0);
   p.m_tiles = (M + TM - 1) / TM;
-  p.n_tiles = (N + TN - 1) / TN;
+  // tile width: 256 columns unless 128-column tiles fill the SM pairs' last wave clearly better
+  int sms0 = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, A.get_device()));
+  const int pairs = std::max(1, sms0 / 2);
+  auto wave_eff = [&](int tn) {
+    const long t = (long)p.m_tiles * ((N + tn - 1) / tn);
+    const long waves = (t + pairs - 1) / pairs;
+    return (double)t / (double)(waves * pairs);
+  };
+  static const int force_tn = [] {
+    const char* e = std::getenv("MESH_PAIR_TN");
+    return e ? std::atoi(e) : 0;
+  }();
+  int tn_sel = 256;
+  if ((tn == 128 || tn == 256) && !(tn == 128 && epi == SILU_BF16))
+    tn_sel = (int)tn;
+  else if ((force_tn == 128 || force_tn == 256) && !(force_tn == 128 && epi == SILU_BF16))
+    tn_sel = force_tn;
+  else if (pair_auto_narrow() && epi == STORE_BF16 && wave_eff(128) > wave_eff(256) * 1.12)
+    tn_sel = 128;
+  p.n_tiles = (N + tn_sel - 1) / tn_sel;
   p.k_blocks = (K + BK - 1) / BK;
   p.err = err.data_ptr<int>();
   static const int spin = [] {
@@ -392,25 +426,28 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 384, "gemm_2sm: trace");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
-  int sms = 0;
-  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, A.get_device()));
-  const int clusters = std::max(1, std::min(p.m_tiles * p.n_tiles, sms / 2));
-  static const int stages = [] {
+  const int clusters = std::max(1, std::min(p.m_tiles * p.n_tiles, pairs));
+  // stages: about 192 KB of operands (6 x 32 KB at TN=256, 8 x 24 KB at TN=128) unless overridden
+  static const int stages_env = [] {
     const char* e = std::getenv("MESH_PAIR_STAGES");
-    const int v = e ? std::atoi(e) : 6;
-    return std::max(2, std::min(v, MAX_STAGES));
+    return e ? std::atoi(e) : 0;
   }();
+  const int stages = std::max(2, std::min(stages_env ? stages_env : (tn_sel == 256 ? 6 : 8), MAX_STAGES));
   p.stages = stages;
-  const size_t smem = smem_bytes(stages);
+  CUtensorMap ta = tma_map_2d_bf16(A.data_ptr(), K, M, A.stride(0), BK, 128);
+  CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, tn_sel / 2);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  auto go = [&](auto kern) {
+  auto go = [&](auto kern, size_t smem) {
+    TORCH_CHECK(smem <= 232448, "gemm_2sm: too many stages for shared memory");
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     C10_CUDA_CHECK(launch_kc(kern, dim3(2 * clusters), dim3(NUM_THREADS), smem, st, 2, ta, tb, p));
   };
   if (epi == SILU_BF16)
-    go(gemm_2sm_kernel<SILU_BF16>);
+    go(gemm_2sm_kernel<SILU_BF16, 256>, smem_bytes<256>(stages));
+  else if (tn_sel == 128)
+    go(gemm_2sm_kernel<STORE_BF16, 128>, smem_bytes<128>(stages));
   else
-    go(gemm_2sm_kernel<STORE_BF16>);
+    go(gemm_2sm_kernel<STORE_BF16, 256>, smem_bytes<256>(stages));
 }
 
 }  // namespace mesh

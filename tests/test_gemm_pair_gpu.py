@@ -17,12 +17,13 @@ def _rel(x, y):
 
 @pytest.mark.parametrize("M,N,K", [(512, 1024, 4096), (256, 256, 64), (700, 800, 1000), (4096, 4096, 512),
                                    (300, 6144, 4096), (1, 32, 64)])
-def test_pair_gemm_store(M, N, K):
+@pytest.mark.parametrize("tn", [0, 256, 128])
+def test_pair_gemm_store(M, N, K, tn):
     from mesh_b200 import ops
     a = _rand(M, K, seed=1)
     b = _rand(N, K, std=0.05, seed=2)
     out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
-    ops.gemm_pair(a, b, out)
+    ops.gemm_pair(a, b, out, tn=tn)
     torch.cuda.synchronize()
     ops.scratch(DEV).check("gemm_pair")
     want = a.float() @ b.float().T
