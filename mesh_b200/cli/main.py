@@ -123,13 +123,22 @@ def cmd_device_init(a):
         print(f"initialised device {d['device_id']} (control plane unreachable: {e})")
 
 
-def cmd_device_status(a):
+def device_status() -> dict:
+    from ..models.registry import ShardRegistry
     d = load_device()
     out = {k: v for k, v in d.items() if k != "private_key"}
     stats = home() / "inference_stats.json"
     if stats.exists():
         out["inference_stats"] = json.loads(stats.read_text())
-    print(json.dumps(out, indent=2))
+    rm = resource_manager()
+    out["resources"] = rm.status()
+    rm.close()
+    out["shards"] = ShardRegistry(home() / "shards").summary()
+    return out
+
+
+def cmd_device_status(a):
+    print(json.dumps(device_status(), indent=2))
 
 
 def cmd_device_start(a):
@@ -198,57 +207,91 @@ def _tp_group_leader(tb, cfg, ecfg, d=None):
 
 
 def cmd_device_runtime(a):
+    """The long-lived worker: rotating file log, the memory commitment (host commitments pinned
+    for the process's life, HBM commitments sizing each GPU's KV pool), the shard registry, then
+    the claim loop over one GPU, a TP group of GPUs, or the CPU oracle."""
+    import logging
+    from ..utils.logs import init_production_logging
+    init_production_logging(getattr(a, "log_level", "info"), home() / "logs")
+    log = logging.getLogger("mesh.runtime")
     d = load_device()
     ring = d.get("ring", {})
     if not ring.get("model_id"):
         raise SystemExit("join a ring first: `mesh ring join --model-id <id>`")
+    rm = resource_manager()
+    hbm_commit = rm.cfg.user_allocated if (rm.is_locked and rm.pool == "hbm") else 0
+    log.info("resource commitment: %s", rm.status())
     b2 = d.get("b200", {})
     tp = int(b2.get("tp", 1))
     model_dir = b2.get("model_dir") or ""
-    if d.get("execution", {}).get("preferred_provider") == "cuda" and (tp > 1 or model_dir):
-        # one process per GPU; rank 0 runs the worker loop and drives the group
-        import functools
-        import tempfile
-        from ..runtime.tp_group import GroupSpec, run_group
-        spec = GroupSpec(world=tp, model_dir=model_dir or None, preset=None if model_dir else ring["model_id"],
-                         max_seq_len=int(b2.get("max_seq_len", 4096)), num_pages=int(b2.get("kv_pages", 4096)),
-                         max_batch=int(b2.get("max_decode_batch", 64)),
-                         use_cuda_graphs=bool(b2.get("cuda_graphs", True)))
-        with tempfile.TemporaryDirectory(dir=str(home())) as wd:
-            run_group(spec, functools.partial(_tp_group_leader, d=d), wd)
-        return
-    coord = build_coordinator(d, ring["model_id"])
-    w = _make_worker(d, coord)
-    w.start()
     try:
-        w.run()
+        if d.get("execution", {}).get("preferred_provider") == "cuda" and (tp > 1 or model_dir):
+            # one process per GPU; rank 0 runs the worker loop and drives the group
+            import functools
+            import tempfile
+            from ..runtime.tp_group import GroupSpec, run_group
+            spec = GroupSpec(world=tp, model_dir=model_dir or None, preset=None if model_dir else ring["model_id"],
+                             max_seq_len=int(b2.get("max_seq_len", 4096)), num_pages=int(b2.get("kv_pages", 4096)),
+                             max_batch=int(b2.get("max_decode_batch", 64)),
+                             use_cuda_graphs=bool(b2.get("cuda_graphs", True)),
+                             registry_dir=str(home() / "shards"), hbm_commit_bytes=hbm_commit)
+            log.info("starting a TP group of %d GPU(s) for %s", tp, ring["model_id"])
+            with tempfile.TemporaryDirectory(dir=str(home())) as wd:
+                run_group(spec, functools.partial(_tp_group_leader, d=d), wd)
+            return
+        coord = build_coordinator(d, ring["model_id"])
+        w = _make_worker(d, coord)
+        w.start()
+        try:
+            w.run()
+        finally:
+            coord.stats.save_to_file(str(home()))
     finally:
-        coord.stats.save_to_file(str(home()))
+        rm.close()
 
 
 # ------------------------------------------------------------------------------------------ resource
 def _parse_mem(s: str) -> int:
-    s = s.strip().upper()
-    mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30, "T": 1 << 40}
-    if s and s[-1] == "B":
-        s = s[:-1]
-    if s and s[-1] in mult:
-        return int(float(s[:-1]) * mult[s[-1]])
-    return int(s)
+    from ..runtime.resources import parse_memory_string
+    return parse_memory_string(s)
+
+
+def resource_manager(pool=None):
+    from ..runtime.resources import ResourceManager
+    return ResourceManager(home() / "resource_lock.toml", pool=pool)
 
 
 def cmd_resource(a):
+    """Commit memory to the mesh (``agent/src/main.rs`` resource commands over the resource
+    manager): ``lock`` records the commitment (per-GPU HBM on a GPU box, host RAM otherwise) with
+    its cooldown; the device runtime pins host commitments and sizes its KV pool from HBM ones."""
+    from ..errors import CooldownActive, MeshError
     d = load_device()
-    if a.action == "lock":
-        d["resource_lock"] = {"memory_bytes": _parse_mem(a.memory), "locked_at": int(time.time())}
-        save_device(d)
-        print(f"locked {d['resource_lock']['memory_bytes']} bytes for the mesh")
-    elif a.action == "unlock":
-        d.pop("resource_lock", None)
-        save_device(d)
-        print("unlocked")
-    else:
-        print(json.dumps(d.get("resource_lock", {"locked": False})))
+    rm = resource_manager(getattr(a, "pool", None))
+    try:
+        if a.action == "lock":
+            rm.set_allocation(_parse_mem(a.memory))
+            rm.lock(pin=False)
+            d["resource_lock"] = {"memory_bytes": rm.cfg.user_allocated, "pool": rm.pool,
+                                  "locked_at": rm.cfg.lock_timestamp}
+            save_device(d)
+            print(f"locked {rm.cfg.user_allocated} bytes of {rm.pool} for the mesh "
+                  f"({rm.cfg.locked_memory} with the 7% margin); unlock allowed after {rm.cfg.cooldown_hours} h")
+        elif a.action == "unlock":
+            rm.unlock()
+            d.pop("resource_lock", None)
+            save_device(d)
+            print("unlocked")
+        else:
+            print(json.dumps(rm.status()))
+    except CooldownActive as e:
+        print(str(e), file=sys.stderr)
+        return 1
+    except MeshError as e:
+        print(f"resource error: {e}", file=sys.stderr)
+        return 1
+    finally:
+        rm.close()
 
 
 # ------------------------------------------------------------------------------------------ ring
@@ -419,27 +462,11 @@ def cmd_doctor(a):
 
 # ------------------------------------------------------------------------------------------ ui
 def cmd_ui(a):
-    """Local API for dashboards (``/api/local/*``); the browser dashboard itself is not shipped."""
+    """Local API for dashboards (``/api/local/*``, the routes of ``agent/src/ui.rs:583-612``); the
+    browser dashboard itself is not shipped."""
     import uvicorn
-    from fastapi import FastAPI
-    app = FastAPI(title="mesh local api")
-
-    @app.get("/api/local/device")
-    def device():
-        d = load_device()
-        return {k: v for k, v in d.items() if k != "private_key"}
-
-    @app.get("/api/local/stats")
-    def stats():
-        p = home() / "inference_stats.json"
-        return json.loads(p.read_text()) if p.exists() else {}
-
-    @app.get("/api/local/topology")
-    def topology():
-        d = load_device()
-        return client(d).topology(d["network_id"], d.get("ring", {}).get("model_id"))
-
-    uvicorn.run(app, host="127.0.0.1", port=a.api_port)
+    from .local_api import create_local_app
+    uvicorn.run(create_local_app(), host="127.0.0.1", port=a.api_port)
 
 
 def build_parser():

@@ -132,6 +132,8 @@ class GroupSpec:
     use_cuda_graphs: bool = True
     first_device: int = 0
     timeout_s: float = 120.0
+    registry_dir: Optional[str] = None   # shard registry each rank records its shard in
+    hbm_commit_bytes: int = 0            # per-GPU commitment: sizes the KV pool when set
 
 
 def build_rank_backend(spec: GroupSpec, rank: int, group=None):
@@ -145,21 +147,43 @@ def build_rank_backend(spec: GroupSpec, rank: int, group=None):
     from ..models.llama import KVPool, LlamaRunner
     dev = torch.device("cuda", spec.first_device + rank)
     torch.cuda.set_device(dev)
+    base = torch.cuda.memory_allocated(dev)
+    registry = shard = None
     if spec.model_dir:
         from ..models.artifacts import assignment_for, load_model_manifest, load_shard, shard_to_device_weights
         man = load_model_manifest(Path(spec.model_dir))
         a = assignment_for(Path(spec.model_dir), man["model_id"], rank, spec.world)
-        cfg, tensors = load_shard(Path(spec.model_dir), a)
+        if spec.registry_dir:
+            from ..models.registry import ShardRegistry
+            registry = ShardRegistry(spec.registry_dir)
+            shard = registry.assign_shard(a).key
+        try:
+            cfg, tensors = load_shard(Path(spec.model_dir), a)
+        except Exception as e:
+            if registry is not None:
+                registry.mark_error(shard, str(e))
+            raise
         w = shard_to_device_weights(cfg, tensors, rank, spec.world, device=dev)
         del tensors
     else:
         from ..models.weights import synthetic_device_weights
         cfg = get_preset(spec.preset or "small")
         w = synthetic_device_weights(cfg, rank, spec.world, seed=spec.seed, device=dev)
+    weight_bytes = torch.cuda.memory_allocated(dev) - base
+    if registry is not None:
+        from ..models.registry import record_shard_load
+        record_shard_load(registry, spec.model_dir, a, weight_bytes, str(dev))
     ecfg = EngineConfig(max_seq_len=spec.max_seq_len, use_cuda_graphs=spec.use_cuda_graphs, tp=spec.world)
-    kv = KVPool(cfg, w.layout.local_kv_heads, spec.num_pages, ecfg.page_size, dev)
+    num_pages = spec.num_pages
+    if spec.hbm_commit_bytes:
+        from .resources import kv_pages_for
+        num_pages = kv_pages_for(spec.hbm_commit_bytes, weight_bytes,
+                                 KVPool.bytes_per_page(cfg, w.layout.local_kv_heads, ecfg.page_size))
+    kv = KVPool(cfg, w.layout.local_kv_heads, num_pages, ecfg.page_size, dev)
     runner = LlamaRunner(w, ecfg, kv, dev, group=group, max_tokens=spec.max_tokens)
-    return GpuBackend(Engine(runner, ecfg, max_batch=spec.max_batch)), cfg, ecfg
+    backend = GpuBackend(Engine(runner, ecfg, max_batch=spec.max_batch))
+    backend.registry, backend.shard_key = registry, shard
+    return backend, cfg, ecfg
 
 
 def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, result_path: Optional[str],
@@ -193,6 +217,8 @@ def _rank_main(rank: int, spec: GroupSpec, init_file: str, leader: Callable, res
             follow(backend, ctl)
         torch.cuda.synchronize()
         backend.eng.close()
+        if getattr(backend, "registry", None) is not None:
+            backend.registry.mark_unloaded(backend.shard_key)
     finally:
         dist.destroy_process_group()
 
