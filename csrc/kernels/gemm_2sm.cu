@@ -362,15 +362,6 @@ bool gemm_2sm_supported(int64_t M, int64_t N, int64_t K, int64_t epi) {
   return M >= 1 && N >= 1 && K >= 1;
 }
 
-// 128-column tiles are picked automatically only with MESH_PAIR_AUTO_TN=1 (until measured)
-static bool pair_auto_narrow() {
-  static const bool v = [] {
-    const char* e = std::getenv("MESH_PAIR_AUTO_TN");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
 void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t epi, at::Tensor& err,
               const c10::optional<at::Tensor>& trace, int64_t tn) {
   using namespace g2sm;
@@ -393,15 +384,8 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
   p.K = K;
   p.ldo = out.stride(0);
   p.m_tiles = (M + TM - 1) / TM;
-  // tile width: 256 columns unless 128-column tiles fill the SM pairs' last wave clearly better
-  int sms0 = 0;
-  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, A.get_device()));
-  const int pairs = std::max(1, sms0 / 2);
-  auto wave_eff = [&](int tn) {
-    const long t = (long)p.m_tiles * ((N + tn - 1) / tn);
-    const long waves = (t + pairs - 1) / pairs;
-    return (double)t / (double)(waves * pairs);
-  };
+  // tile width: 256 columns. 128-column tiles (argument or MESH_PAIR_TN=128) fill a short last
+  // wave better but move half again as many operand bytes per FLOP and measured 37-46 % slower.
   static const int force_tn = [] {
     const char* e = std::getenv("MESH_PAIR_TN");
     return e ? std::atoi(e) : 0;
@@ -411,8 +395,6 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
     tn_sel = (int)tn;
   else if ((force_tn == 128 || force_tn == 256) && !(force_tn == 128 && epi == SILU_BF16))
     tn_sel = force_tn;
-  else if (pair_auto_narrow() && epi == STORE_BF16 && wave_eff(128) > wave_eff(256) * 1.12)
-    tn_sel = 128;
   p.n_tiles = (N + tn_sel - 1) / tn_sel;
   p.k_blocks = (K + BK - 1) / BK;
   p.err = err.data_ptr<int>();
@@ -426,6 +408,9 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->numel() >= 384, "gemm_2sm: trace");
     p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, A.get_device()));
+  const int pairs = std::max(1, sms / 2);
   const int clusters = std::max(1, std::min(p.m_tiles * p.n_tiles, pairs));
   // stages: about 192 KB of operands (6 x 32 KB at TN=256, 8 x 24 KB at TN=128) unless overridden
   static const int stages_env = [] {

@@ -129,7 +129,6 @@ class GpuBackend:
     def decode(self, items):
         e = self.eng
         sids = [self.map[h] for h, *_ in items]
-        before = {sid: len(e.sessions[sid].generated) + (1 if False else 0) for sid in sids}
         e.decode_step(only=set(sids))
         e.flush_history()
         out = []
@@ -137,6 +136,10 @@ class GpuBackend:
             g = e.sessions[sid].generated
             out.append(g[-1])
         return out
+
+    def drain_counters(self) -> Dict[str, float]:
+        """Engine counters since the last call (layers, collectives, bytes, kernel launches)."""
+        return self.eng.drain_counters()
 
     def release(self, h):
         sid = self.map.pop(h, None)

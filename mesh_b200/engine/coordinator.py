@@ -260,11 +260,18 @@ class InferenceCoordinator:
         self.stats.add("total_prompt_tokens", len(sess.request.prompt_tokens))
         self.stats.add("total_tokens_generated", 1)
         self.stats.add("device_prefill_time_ms", (time.perf_counter() - t0) * 1e3)
+        self._drain_backend_counters()
         self.sched.update(sess.handle, sess.kv_tokens, self.backend.token_ceiling(sess.kv_tokens))
         if sess.complete:
             self.sched.set_complete(sess.handle, True)
         else:
             self.sched.enqueue(sess.handle)
+
+    def _drain_backend_counters(self) -> None:
+        drain = getattr(self.backend, "drain_counters", None)
+        if drain is not None:
+            for k, v in drain().items():
+                self.stats.add(k, v)
 
     def build_next_decode_batch(self, primary_session: Optional[str] = None) -> DecodeBatchPlan:
         h = self.sessions[primary_session].handle if primary_session in self.sessions else -1
@@ -283,6 +290,7 @@ class InferenceCoordinator:
         items = [(s.handle, s.request.config.temperature, s.request.config.top_p,
                   s.request.seed_for_position(0)) for s in sess]
         toks = self.backend.decode(items)
+        self._drain_backend_counters()
         st = self.stats
         st.add("decode_microbatches_executed")
         st.add("decode_sessions_batched", len(sess))

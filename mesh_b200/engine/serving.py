@@ -229,6 +229,37 @@ class Engine:
         self.steps = 0
         self.stats = dict(prefill_tokens=0, decode_tokens=0, decode_steps=0, prefill_chunks=0,
                           peak_batch_size=0)
+        # reference inference-stats keys this engine feeds (GpuBackend drains them into the
+        # coordinator's InferenceStats): layers, collectives and their NVLink bytes, kernel launches
+        self.counters: Dict[str, float] = {}
+        from .. import ops
+        self._launch_mark = ops.LAUNCHES[0]
+
+    def _account(self, tokens: int) -> None:
+        """Count one forward over ``tokens`` rows: two tensor-parallel all-reduces per layer, each
+        a device-resident collective that moves (world-1) partial [tokens, H] bf16 rows per rank."""
+        from .. import ops
+        r = self.runner
+        L, w = self.cfg.num_layers, r.world
+        c = self.counters
+        add = lambda k, v: c.__setitem__(k, c.get(k, 0) + v)
+        add("total_layers_processed", L)
+        add("kernel_launches", ops.LAUNCHES[0] - self._launch_mark)
+        self._launch_mark = ops.LAUNCHES[0]
+        if w > 1:
+            n = 2 * L
+            moved = n * tokens * r.H * 2 * (w - 1)
+            add("allreduce_operations", n)
+            add("total_collective_operations", n)
+            add("total_device_resident_collectives", n)
+            add("total_collective_worker_participants", n * w)
+            add("fused_allreduce_operations" if r.use_fused_ar else "nccl_allreduce_operations", n)
+            add("total_collective_bytes_sent", moved)
+            add("total_collective_bytes_received", moved)
+
+    def drain_counters(self) -> Dict[str, float]:
+        out, self.counters = self.counters, {}
+        return out
 
     # ----------------------------------------------------------------------------- requests
     def submit(self, prompt: List[int], max_new_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
@@ -363,6 +394,7 @@ class Engine:
             self.hist_first.append(([s.sid for s in finished_prompts], toks))
         self.stats["prefill_tokens"] += T
         self.stats["prefill_chunks"] += 1
+        self._account(T)
         for s in finished_prompts:
             if s.done:
                 self._retire(s)
@@ -439,6 +471,7 @@ class Engine:
         self.hist_rows.append(mapping)
         self.stats["decode_tokens"] += len(act)
         self.stats["decode_steps"] += 1
+        self._account(b)
         self.stats["peak_batch_size"] = max(self.stats["peak_batch_size"], len(act))
         for s in act:
             if s.done:

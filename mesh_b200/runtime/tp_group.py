@@ -69,6 +69,10 @@ class TPGroupBackend:
     def release(self, h):
         return self._call("release", h)
 
+    def drain_counters(self):
+        # local bookkeeping only: nothing is announced, the followers keep their own counters
+        return self.b.drain_counters() if hasattr(self.b, "drain_counters") else {}
+
     def kv_bytes(self, h) -> int:
         # every rank holds the same number of pages for a session (its own KV heads)
         return self.b.kv_bytes(h) * self.world

@@ -37,6 +37,11 @@ def test_gpu_coordinator_microbatches_equal_solo_runs():
         c.submit(r)
     res = {r.job_id: r.generated_tokens for r in c.run_until_idle()}
     assert c.stats.get("decode_batch_capacity_deferrals") >= 1  # 3 sessions, batches of 2
+    # the engine's counters reach the reference stats keys (one rank: no collectives)
+    L = eng.cfg.num_layers
+    steps = c.stats.get("decode_microbatches_executed")
+    assert c.stats.get("total_layers_processed") >= L * (steps + 3)  # 3 prefills + decode steps
+    assert c.stats.get("kernel_launches") > 0 and c.stats.get("allreduce_operations") == 0
     solo = [InferenceCoordinator(GpuBackend(eng)).process_inference(_req(p, 5)).generated_tokens for p in prompts]
     assert [res[r.job_id] for r in reqs] == solo
     eng.close()
