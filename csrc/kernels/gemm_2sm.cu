@@ -32,12 +32,20 @@ namespace g2sm {
 constexpr int TM = 256;                        // output rows per SM pair (128 per CTA)
 constexpr int BK = 64;                         // k elements per stage (one 128-byte swizzle atom)
 constexpr uint32_t A_BYTES = 128 * BK * 2;     // one CTA's 128 rows of A for one stage
-// Tile width TN (256 or 128 output columns per pair): each CTA stages TN/2 rows of B per stage.
+// Tile width TN (128, 256 or 512 output columns per pair). Up to 256 columns one MMA of N = TN per
+// 16-wide k step and two accumulators (the epilogue of a tile overlaps the next mainloop); 512
+// columns issue two N = 256 MMAs that share the A stage (a quarter less operand traffic per FLOP)
+// into one accumulator that fills TMEM, so the epilogue does not overlap.
 template <int TN>
 struct Tile {
-  static constexpr uint32_t B_BYTES = (TN / 2) * BK * 2;
+  static constexpr int NSUB = TN == 512 ? 2 : 1;                // MMAs per 16-wide k step
+  static constexpr int MMA_N = TN / NSUB;
+  static constexpr int BROWS = MMA_N / 2;                       // rows of B per CTA per MMA
+  static constexpr uint32_t B_SUB_BYTES = BROWS * BK * 2;
+  static constexpr uint32_t B_BYTES = NSUB * B_SUB_BYTES;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * TN;  // two accumulators
+  static constexpr int NACC = TN == 512 ? 1 : 2;                // accumulators in TMEM
+  static constexpr uint32_t TMEM_COLS = NACC * TN;
 };
 constexpr int MAX_STAGES = 9;                  // 24 KB stages (TN = 128) fit 9 times
 constexpr int NUM_THREADS = 192;
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = cluster; t < tiles && ok; t += nclusters) {
         int tm, tn;
         tile_mn(t, p, tm, tn);
-        const int arow = tm * TM + (int)rank * 128, brow = tn * TN + (int)rank * (TN / 2);
+        const int arow = tm * TM + (int)rank * 128, brow = tn * TN + (int)rank * Tile<TN>::BROWS;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           // the leader learns from its MMA commit that both CTAs' copies of the stage were consumed
           // and passes that on to the peer's producer (a plain remote arrive)
@@ -197,7 +205,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
           uint8_t* st = stages + (size_t)stage * STAGE_BYTES;
           tma_load_2d_pair(st, &tmA, full, kb * BK, arow, pol_a);
-          tma_load_2d_pair(st + A_BYTES, &tmB, full, kb * BK, brow, pol_b);
+#pragma unroll
+          for (int h = 0; h < Tile<TN>::NSUB; ++h)
+            tma_load_2d_pair(st + A_BYTES + h * Tile<TN>::B_SUB_BYTES, &tmB, full, kb * BK,
+                             brow + h * Tile<TN>::MMA_N, pol_b);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -215,15 +226,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // -------------------------------- MMA issuer (leader only) --------------------------------
     if (rank == 0) {
-      constexpr uint32_t IDESC = make_idesc_bf16(TM, TN);
+      constexpr uint32_t IDESC = make_idesc_bf16(TM, Tile<TN>::MMA_N);
       long mma_seq = 0;
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int t = cluster; t < tiles && ok; t += nclusters, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        const int acc = it % Tile<TN>::NACC;
+        const uint32_t acc_phase = (uint32_t)(it / Tile<TN>::NACC) & 1u;
         int w = 1;
         if (lane == 0) w = wait_bar(&bars->tempty[acc], acc_phase ^ 1u, p.err, ERR_MBAR_TIMEOUT_MMA, abort_flag, p.spin);
         if (!__shfl_sync(0xffffffffu, w, 0)) {
@@ -243,9 +254,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(stages + (size_t)stage * STAGE_BYTES);
-            const uint64_t ad = make_sdesc_sw128(a_addr), bd = make_sdesc_sw128(a_addr + A_BYTES);
+            const uint64_t ad = make_sdesc_sw128(a_addr);
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) umma_pair(d, ad + 2 * k, bd + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k)
+#pragma unroll
+              for (int h = 0; h < Tile<TN>::NSUB; ++h)
+                umma_pair(d + (uint32_t)(h * Tile<TN>::MMA_N), ad + 2 * k,
+                          make_sdesc_sw128(a_addr + A_BYTES + h * Tile<TN>::B_SUB_BYTES) + 2 * k, IDESC,
+                          (kb > 0 || k > 0) ? 1u : 0u);
             // the stage is free once these MMAs are done (the producer relays it to the peer)
             umma_commit_pair(smem_u32(&bars->empty[stage]));
           }
@@ -278,11 +294,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int et = threadIdx.x - 64;
     int it = 0;
     for (int t = cluster; t < tiles; t += nclusters, ++it) {
-      const int acc = it & 1;
+      const int acc = it % Tile<TN>::NACC;
       if (et == 0) {
         // the leader sees the MMA commit and passes the accumulator on to the peer's epilogue
-        const bool w =
-            wait_bar(&bars->tfull[acc], (uint32_t)(it >> 1) & 1u, p.err, ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag, p.spin);
+        const bool w = wait_bar(&bars->tfull[acc], (uint32_t)(it / Tile<TN>::NACC) & 1u, p.err,
+                                ERR_MBAR_TIMEOUT_EPILOGUE, abort_flag, p.spin);
         if (w && rank == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bars->tfull[acc]), 1));
         bars->epi_ok = w ? 1 : 0;
       }
@@ -385,15 +401,17 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
   p.ldo = out.stride(0);
   p.m_tiles = (M + TM - 1) / TM;
   // tile width: 256 columns. 128-column tiles (argument or MESH_PAIR_TN=128) fill a short last
-  // wave better but move half again as many operand bytes per FLOP and measured 37-46 % slower.
+  // wave better but move half again as many operand bytes per FLOP and measured 37-46 % slower;
+  // 512-column tiles (argument or MESH_PAIR_TN=512) move a quarter fewer.
   static const int force_tn = [] {
     const char* e = std::getenv("MESH_PAIR_TN");
     return e ? std::atoi(e) : 0;
   }();
+  auto valid_tn = [&](int v) { return (v == 128 || v == 256 || v == 512) && !(v == 128 && epi == SILU_BF16); };
   int tn_sel = 256;
-  if ((tn == 128 || tn == 256) && !(tn == 128 && epi == SILU_BF16))
+  if (valid_tn((int)tn))
     tn_sel = (int)tn;
-  else if ((force_tn == 128 || force_tn == 256) && !(force_tn == 128 && epi == SILU_BF16))
+  else if (valid_tn(force_tn))
     tn_sel = force_tn;
   p.n_tiles = (N + tn_sel - 1) / tn_sel;
   p.k_blocks = (K + BK - 1) / BK;
@@ -417,18 +435,24 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
     const char* e = std::getenv("MESH_PAIR_STAGES");
     return e ? std::atoi(e) : 0;
   }();
-  const int stages = std::max(2, std::min(stages_env ? stages_env : (tn_sel == 256 ? 6 : 8), MAX_STAGES));
+  const int max_st = tn_sel == 512 ? 4 : MAX_STAGES;  // 48 KB stages at 512 columns
+  const int def_st = tn_sel == 512 ? 4 : (tn_sel == 256 ? 6 : 8);
+  const int stages = std::max(2, std::min(stages_env ? stages_env : def_st, max_st));
   p.stages = stages;
   CUtensorMap ta = tma_map_2d_bf16(A.data_ptr(), K, M, A.stride(0), BK, 128);
-  CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, tn_sel / 2);
+  CUtensorMap tb = tma_map_2d_bf16(B.data_ptr(), K, N, B.stride(0), BK, tn_sel == 512 ? 128 : tn_sel / 2);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto go = [&](auto kern, size_t smem) {
     TORCH_CHECK(smem <= 232448, "gemm_2sm: too many stages for shared memory");
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     C10_CUDA_CHECK(launch_kc(kern, dim3(2 * clusters), dim3(NUM_THREADS), smem, st, 2, ta, tb, p));
   };
-  if (epi == SILU_BF16)
+  if (epi == SILU_BF16 && tn_sel == 512)
+    go(gemm_2sm_kernel<SILU_BF16, 512>, smem_bytes<512>(stages));
+  else if (epi == SILU_BF16)
     go(gemm_2sm_kernel<SILU_BF16, 256>, smem_bytes<256>(stages));
+  else if (tn_sel == 512)
+    go(gemm_2sm_kernel<STORE_BF16, 512>, smem_bytes<512>(stages));
   else if (tn_sel == 128)
     go(gemm_2sm_kernel<STORE_BF16, 128>, smem_bytes<128>(stages));
   else

@@ -225,6 +225,7 @@ def gemmcmp(args):
     runs = {"pair": lambda i: ops.gemm_pair(a, bs[i % nc], out),
             "pair256": lambda i: ops.gemm_pair(a, bs[i % nc], out, tn=256),
             "pair128": lambda i: ops.gemm_pair(a, bs[i % nc], out, tn=128),
+            "pair512": lambda i: ops.gemm_pair(a, bs[i % nc], out, tn=512),
             "one_sm": lambda i: ops.gemm(a, bs[i % nc], out, ops.EPI_STORE_BF16, trans=False),
             "cublas": lambda i: torch.mm(a, bs[i % nc].t(), out=out)}
     for name in args.impls:

@@ -183,8 +183,8 @@ def gemm_pair(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EP
               trace: Optional[torch.Tensor] = None, tn: int = 0) -> torch.Tensor:
     """out = x @ w.T (EPI_SILU_BF16: SiLU(gate) * up of the interleaved gate/up product) on SM pairs.
     trace: optional int64 [384] of %globaltimer stamps for the first pair (producer empty-waits of both
-    CTAs, then the MMA thread's full-waits). tn: tile width (256 or 128 output columns per SM pair;
-    0 picks the one whose last wave fills the pairs better)."""
+    CTAs, then the MMA thread's full-waits). tn: tile width (128, 256 or 512 output columns per SM
+    pair; 0: the default, 256, or ``MESH_PAIR_TN``)."""
     if tn:
         ext().gemm_2sm(x, w, out, epi, scratch(x.device).err, trace, tn)
     else:

@@ -17,7 +17,7 @@ def _rel(x, y):
 
 @pytest.mark.parametrize("M,N,K", [(512, 1024, 4096), (256, 256, 64), (700, 800, 1000), (4096, 4096, 512),
                                    (300, 6144, 4096), (1, 32, 64)])
-@pytest.mark.parametrize("tn", [0, 256, 128])
+@pytest.mark.parametrize("tn", [0, 256, 128, 512])
 def test_pair_gemm_store(M, N, K, tn):
     from mesh_b200 import ops
     a = _rand(M, K, seed=1)
@@ -32,7 +32,8 @@ def test_pair_gemm_store(M, N, K, tn):
 
 
 @pytest.mark.parametrize("M,I,K", [(512, 1792, 4096), (640, 128, 1024)])
-def test_pair_gemm_silu(M, I, K):
+@pytest.mark.parametrize("tn", [0, 512])
+def test_pair_gemm_silu(M, I, K, tn):
     """Gate/up rows interleaved in 64-row blocks (the serving layout); out = SiLU(gate) * up."""
     from mesh_b200 import ops
     from mesh_b200.models.weights import interleave_gate_up
@@ -41,7 +42,7 @@ def test_pair_gemm_silu(M, I, K):
     up = _rand(I, K, std=0.05, seed=5)
     w = interleave_gate_up(gate, up, I)
     out = torch.full((M, I), float("nan"), dtype=torch.bfloat16, device=DEV)
-    ops.gemm_pair(a, w, out, ops.EPI_SILU_BF16)
+    ops.gemm_pair(a, w, out, ops.EPI_SILU_BF16, tn=tn)
     torch.cuda.synchronize()
     ops.scratch(DEV).check("gemm_pair silu")
     g = a.float() @ gate.float().T
