@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-nvls", action="store_true",
                     help="keep the fused all-reduce on plain peer loads (no NVSwitch multimem) at every TP degree")
+    ap.add_argument("--prefill-overlap", action="store_true",
+                    help="TP prefill: two halves of each chunk on two streams (all-reduce of one overlaps GEMMs of the other)")
     ap.add_argument("--ar-impl", default="auto",
                     choices=["auto", "unfused", "gemm_ar", "oneshot", "twoshot", "push", "push_oneshot", "nccl"],
                     help="TP all-reduce: auto/unfused (separate peer-memory kernel fused with residual + RMSNorm), "
@@ -142,7 +144,8 @@ def main():
     max_seq = (P + G + 15) // 16 * 16
     ecfg = EngineConfig(tp=world, max_seq_len=max_seq, prefill_chunk_tokens=args.prefill_chunk,
                         use_cuda_graphs=not args.no_graphs, max_decode_batch_size=S,
-                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl, nvls=not args.no_nvls)
+                        allreduce_impl="nccl" if args.impl == "nccl" else args.ar_impl, nvls=not args.no_nvls,
+                        prefill_overlap=args.prefill_overlap or EngineConfig().prefill_overlap)
     w = synthetic_device_weights(cfg, rank, world, seed=1234, device=dev)
     pages = S * (max_seq // 16) + 64
     kv = KVPool(cfg, w.layout.local_kv_heads, pages, 16, dev)
@@ -228,6 +231,7 @@ def main():
                        "global_batch": S, "seq_len": P, "gen_tokens": G, "kv_page_tokens": 16,
                        "parallelism": f"tp{world}", "prefill_chunk_tokens": args.prefill_chunk,
                        "cuda_graphs": not args.no_graphs, "allreduce": "nccl" if args.impl in ("nccl", "torch") else args.ar_impl,
+                       "prefill_overlap": bool(getattr(runner, "overlap_prefill", False)),
                        "nvls": (not args.no_nvls) and world >= 8 and args.impl == "mesh",
                        "l2": "inputs larger than L2 (weights %.1f GB per rank re-read every step)" % (w.nbytes() / 1e9)},
             "e2e": {"value": round(e2e, 1), "unit": "generated tokens/s through Engine.submit/run incl. prefill, "

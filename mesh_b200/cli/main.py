@@ -115,9 +115,18 @@ def cmd_device_init(a):
                   "max_decode_batch": 64, "cuda_graphs": True, "model_dir": a.model_dir or ""}}
     save_device(d)
     try:
-        client(d).register(device_id=d["device_id"], network_id=a.network_id, name=a.name, tier=cap["tier"],
-                           provider=d["execution"]["preferred_provider"], public_key=pub,
-                           capabilities=cap)
+        r = client(d).register(device_id=d["device_id"], network_id=a.network_id, name=a.name, tier=cap["tier"],
+                               provider=d["execution"]["preferred_provider"], public_key=pub,
+                               capabilities=cap)
+        if isinstance(r, dict) and r.get("certificate"):
+            # keep the certificate the control plane issued, after checking it names this device's key
+            from ..control_plane.certificate import verify_certificate
+            cert = verify_certificate(bytes.fromhex(r["certificate"]), bytes.fromhex(r["control_plane_public_key"]))
+            if cert.public_key.hex() != pub or cert.device_id != d["device_id"]:
+                raise SystemExit("the control plane's certificate does not name this device and key")
+            d["certificate"] = r["certificate"]
+            d["control_plane_public_key"] = r["control_plane_public_key"]
+            save_device(d)
         print(f"registered device {d['device_id']} with {a.control_plane}")
     except Exception as e:
         print(f"initialised device {d['device_id']} (control plane unreachable: {e})")

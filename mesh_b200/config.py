@@ -11,6 +11,7 @@ reference (``forward_pass.rs:1280``).
 from __future__ import annotations
 
 import dataclasses
+import os
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -153,6 +154,9 @@ class EngineConfig:
     # it is used from 8 ranks up, where it measured faster (TP8 decode 23.98k vs 22.74k tok/s),
     # while 2 ranks measured equal and plain peer loads stay the default below 8
     nvls: bool = True
+    # TP prefill: run a chunk of several prompts as two halves on two streams so one half's
+    # all-reduces overlap the other half's GEMMs (each half needs >= 512 tokens)
+    prefill_overlap: bool = field(default_factory=lambda: os.environ.get("MESH_PREFILL_OVERLAP", "0") == "1")
     extra: dict = field(default_factory=dict)
 
     def bucket_for(self, batch: int) -> int:

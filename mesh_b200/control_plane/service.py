@@ -76,9 +76,13 @@ def _uid() -> str:
 
 
 class ControlPlane:
-    def __init__(self, db: Optional[Database] = None, model_store: Optional[str] = None):
+    def __init__(self, db: Optional[Database] = None, model_store: Optional[str] = None, key_path: Optional[str] = None):
+        from .certificate import ControlPlaneKeypair
         self.db = db or Database()
         self.model_store = model_store
+        # signs device certificates at registration; MESH_CONTROL_PLANE_KEY names a key file to keep
+        key_path = key_path or os.environ.get("MESH_CONTROL_PLANE_KEY")
+        self.keypair = ControlPlaneKeypair.load_or_generate(key_path) if key_path else ControlPlaneKeypair.generate()
         self.stale_timeout_s = float(os.environ.get("MESHNET_PRESENCE_STALE_TIMEOUT_MS", "15000")) / 1000.0
 
     # ------------------------------------------------------------------------------------ models
@@ -158,6 +162,26 @@ class ControlPlane:
     def register_device(self, device_id: str, network_id: Optional[str], name: str = "", tier: str = "tier2",
                         provider: str = "cpu", contributed_memory: int = 0, capabilities: dict = None,
                         public_key: str = "", certificate: str = "", tensor_plane_addr: str = "") -> dict:
+        """Register (or re-register) a device. With its ed25519 public key (64 hex characters) the
+        control plane issues a signed 30-day certificate (``certificate.py``) and returns it with
+        its own public key; a device-supplied ``certificate`` is ignored."""
+        if not device_id:
+            raise ApiError("device_id cannot be empty")
+        if network_id is not None:
+            if not network_id:
+                raise ApiError("network_id cannot be empty")
+            if not self.db.query("SELECT 1 FROM networks WHERE network_id=?", (network_id,)):
+                raise NotFound(f"network {network_id} not found")
+        cert_hex = ""
+        if public_key:
+            try:
+                pk = bytes.fromhex(public_key)
+            except ValueError:
+                raise ApiError("public_key must be hex")
+            if len(pk) != 32:
+                raise ApiError("public_key must be 32 bytes (Ed25519)")
+            cert_hex = self.keypair.generate_certificate(device_id, network_id or "", pk).hex()
+        certificate = cert_hex
         with self.db.tx() as c:
             c.execute("""INSERT INTO devices (device_id, network_id, name, public_key, certificate, tier, provider,
                          contributed_memory, status, last_heartbeat, created_at, capabilities, tensor_plane_addr)
@@ -169,7 +193,10 @@ class ControlPlane:
                          tensor_plane_addr=excluded.tensor_plane_addr""",
                       (device_id, network_id, name, public_key, certificate, tier, provider, contributed_memory,
                        _now(), _now(), dumps(capabilities or {}), tensor_plane_addr))
-        return {"device_id": device_id, "status": "online"}
+            c.execute("UPDATE devices SET public_key=?, certificate=? WHERE device_id=?",
+                      (public_key, certificate, device_id))
+        return {"device_id": device_id, "status": "online", "certificate": certificate,
+                "control_plane_public_key": self.keypair.public_key().hex()}
 
     def heartbeat(self, device_id: str, throughput_tps: Optional[float] = None) -> dict:
         with self.db.tx() as c:

@@ -355,7 +355,7 @@ class Engine:
         m = StepMeta(ids=pin(ids, torch.int32), pos=pin(pos, torch.int32), slot=pin(slot, torch.int64),
                      block_tables=torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True),
                      seq_lens=pin(klen, torch.int32), cu_q=pin(cu, torch.int32), last_idx=pin(last, torch.int64),
-                     max_q_len=max(b - a for _, a, b in items), decode=False)
+                     max_q_len=max(b - a for _, a, b in items), decode=False, cu_host=cu)
         sampled = [i for i, (s, a, b) in enumerate(items)
                    if s.temperature > 0.0 and s.top_p > 0.0 and b == len(s.prompt)]
         if sampled:

@@ -21,7 +21,7 @@ from __future__ import annotations
 import math
 import os
 from dataclasses import dataclass
-from typing import Optional
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
@@ -45,6 +45,11 @@ def _nvtx_range(name):
         torch.cuda.nvtx.range_pop()
     else:
         torch.cuda.nvtx.range_push(name)
+
+
+# Smallest half of a prefill chunk that runs overlapped with the other half (the SM-pair GEMM's
+# minimum, so neither half falls back to the one-SM kernel's shared stream-K workspace).
+PREFILL_SPLIT_MIN_TOKENS = 512
 
 
 class KVPool:
@@ -80,6 +85,7 @@ class StepMeta:
     top_p: Optional[torch.Tensor] = None
     thr: Optional[torch.Tensor] = None
     nucleus: bool = True   # some row has 0 < top_p < 1 (the sampler's radix passes are needed)
+    cu_host: Optional[List[int]] = None  # host copy of cu_q (prefill): lets the runner split the chunk
 
 
 class LlamaRunner:
@@ -119,6 +125,20 @@ class LlamaRunner:
         if self.use_fused_ar:
             from ..parallel.symm import SymmWorkspace
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
+        # Prefill overlap: a chunk of several prompts runs as two halves on two streams, each with its
+        # own symmetric workspace, so one half's all-reduces (NVLink, a few SMs) run while the other
+        # half's GEMMs hold the tensor cores. Only with the peer-memory all-reduce (NCCL calls on two
+        # streams could be ordered differently on different ranks) and when both halves are big
+        # enough for the SM-pair GEMM, which uses no shared workspace.
+        self.overlap_prefill = (self.use_fused_ar and not self.push_rs and bool(ecfg.prefill_overlap)
+                                and max_tokens >= 2 * PREFILL_SPLIT_MIN_TOKENS)
+        self.symm2 = None
+        self._streams = None
+        self.split_steps = 0
+        if self.overlap_prefill:
+            from ..parallel.symm import SymmWorkspace
+            self.symm2 = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
+            self._streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
         # vocabulary-parallel embedding: this rank's rows live in a table every peer maps, and each
         # token's row is read from its owner (one launch, fused with the first RMSNorm)
         self.emb_table = None
@@ -135,9 +155,10 @@ class LlamaRunner:
         self.last_logits = None
 
     # ------------------------------------------------------------------------------------------
-    def _resid_normed(self, T: int):
-        if self.symm is not None:
-            return self.symm.resid(T), self.symm.normed(T)
+    def _resid_normed(self, T: int, symm=None):
+        symm = symm or self.symm
+        if symm is not None:
+            return symm.resid(T), symm.normed(T)
         return (torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device),
                 torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device))
 
@@ -157,17 +178,18 @@ class LlamaRunner:
         return T * self.H * 2 * (self.world - 1) > (8 << 20)
 
     def _reduce(self, part: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor, gamma: torch.Tensor,
-                parity: int):
+                parity: int, symm=None):
         """resid += sum_ranks(part); normed = RMSNorm(resid) * gamma."""
         T = resid.shape[0]
         eps = self.cfg.rms_norm_eps
+        symm = symm or self.symm
         if self.world == 1:
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
         elif self.push_rs:
-            self.symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout)
+            symm.push_reduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout)
         elif self.use_fused_ar:
-            self.symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout,
-                                           multicast=self.world >= 8)
+            symm.fused_allreduce_norm(T, parity, gamma, eps, two_shot=self._two_shot(T), timeout_s=self.ar_timeout,
+                                      multicast=self.world >= 8)
         else:  # NCCL baseline
             dist.all_reduce(part, group=self.group)
             ops.add_rmsnorm(resid, gamma, normed, eps, delta=part)
@@ -175,52 +197,39 @@ class LlamaRunner:
     def _push(self, T: int, parity: int):
         return self.symm.push_args(T, parity, self._two_shot(T)) if self.push_rs else None
 
-    def _part_buf(self, T: int, parity: int, scratch: dict) -> torch.Tensor:
+    def _part_buf(self, T: int, parity: int, scratch: dict, symm=None) -> torch.Tensor:
         if self.use_fused_ar:
-            return self.symm.partial(parity, T)
+            return (symm or self.symm).partial(parity, T)
         key = ("part", T)
         if key not in scratch:
             scratch[key] = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
         return scratch[key]
 
     def _proj_reduce(self, x: torch.Tensor, wt: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor,
-                     gamma: torch.Tensor, parity: int, bufs: dict):
+                     gamma: torch.Tensor, parity: int, bufs: dict, symm=None):
         """resid += sum_ranks(x @ wt.T); normed = RMSNorm(resid) * gamma (row-parallel projection)."""
         T = x.shape[0]
         if self.gemm_ar and T <= ops.SWAP_AB_MAX_TOKENS:
             self.symm.gemm_allreduce_norm(x, wt, parity, gamma, self.cfg.rms_norm_eps, timeout_s=self.ar_timeout,
                                           multicast=self.world >= 8)
             return
-        part = self._part_buf(T, parity, bufs)
+        part = self._part_buf(T, parity, bufs, symm)
         ops.linear(x, wt, out=part, push=self._push(T, parity))
-        self._reduce(part, resid, normed, gamma, parity)
+        self._reduce(part, resid, normed, gamma, parity, symm)
 
     # ------------------------------------------------------------------------------------------
-    def forward(self, m: StepMeta, bufs: Optional[dict] = None) -> torch.Tensor:
-        """Run all layers and the LM head; returns next-token ids [S] (int32, greedy)."""
+    def _embed(self, m: StepMeta, resid: torch.Tensor, normed: torch.Tensor) -> None:
         c, w = self.cfg, self.w
-        bufs = {} if bufs is None else bufs
-        T = m.ids.shape[0]
-        if T > self.max_tokens:
-            raise ValueError(f"step of {T} tokens exceeds runner capacity {self.max_tokens}")
-
-        def buf(name, shape, dtype=torch.bfloat16):
-            key = (name, tuple(shape), dtype)
-            t = bufs.get(key)
-            if t is None:
-                t = bufs[key] = torch.empty(shape, dtype=dtype, device=self.device)
-            return t
-
-        resid, normed = self._resid_normed(T)
-        rng = _nvtx_range
         if self.emb_table is not None:
             ops.embed_peer_norm(self.emb_table.bases, m.ids, c.vocab_size, w.layers[0].attn_norm, c.rms_norm_eps,
                                 resid, normed)
         else:
             ops.embedding(m.ids, w.embedding, resid)
             ops.add_rmsnorm(resid, w.layers[0].attn_norm, normed, c.rms_norm_eps)
-        qkv_w = (self.hq + 2 * self.hkv) * self.D
-        qkv = buf("qkv", (T, qkv_w))
+
+    def _scratch(self, T: int, buf) -> tuple:
+        w = self.w
+        qkv = buf("qkv", (T, (self.hq + 2 * self.hkv) * self.D))
         q = buf("q", (T, self.hq * self.D))
         attn = buf("attn", (T, self.hq * self.D))
         h = buf("h", (T, w.i_pad))
@@ -229,24 +238,112 @@ class LlamaRunner:
             # output shows up as NaN in the result instead of reusing the previous step's values
             for t in (qkv, q, attn, h):
                 t.fill_(float("nan"))
-        parity = 0
-        for li, L in enumerate(w.layers):
+        return qkv, q, attn, h
+
+    def _layer(self, li: int, m: StepMeta, resid, normed, scr: tuple, bufs: dict, symm=None) -> None:
+        """One decoder layer; ``normed`` holds this layer's attention-normed input on entry and the
+        next layer's (or the final norm's) on exit. Each layer runs two all-reduces, so the
+        partial-buffer parity is the same (0 then 1) in every layer."""
+        w = self.w
+        L = w.layers[li]
+        qkv, q, attn, h = scr
+        kc, vc = self.kv.k[li], self.kv.v[li]
+        ops.qkv_rope(normed, L.wqkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv, qkv_buf=qkv)
+        if m.decode:
+            ops.attn_decode(q, kc, vc, m.block_tables, m.seq_lens, attn, self.scale, self.window,
+                            max_len_hint=m.max_q_len)
+        else:
+            ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
+                             self.window)
+        self._proj_reduce(attn, L.wo, resid, normed, L.mlp_norm, 0, bufs, symm)
+        ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
+        gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
+        self._proj_reduce(h, L.wdown, resid, normed, gamma, 1, bufs, symm)
+
+    def _split_point(self, m: StepMeta) -> int:
+        """Number of prompts in the first half of a prefill chunk run as two overlapped halves, or 0
+        to run it whole: the prompt boundary closest to half the tokens that leaves both halves
+        at least PREFILL_SPLIT_MIN_TOKENS tokens."""
+        if not self.overlap_prefill or m.decode or m.cu_host is None or len(m.cu_host) < 3:
+            return 0
+        cu = m.cu_host
+        T = cu[-1]
+        best, best_d = 0, None
+        for k in range(1, len(cu) - 1):
+            a = cu[k]
+            if a >= PREFILL_SPLIT_MIN_TOKENS and T - a >= PREFILL_SPLIT_MIN_TOKENS:
+                d = abs(2 * a - T)
+                if best_d is None or d < best_d:
+                    best, best_d = k, d
+        return best
+
+    @staticmethod
+    def _sub_meta(m: StepMeta, k0: int, k1: int) -> StepMeta:
+        """Prompts [k0, k1) of a prefill chunk as a step of their own (row and index tensors rebased)."""
+        cu = m.cu_host
+        r0, r1 = cu[k0], cu[k1]
+        cu_q = m.cu_q[k0:k1 + 1] if r0 == 0 else m.cu_q[k0:k1 + 1] - r0
+        last = None if m.last_idx is None else (m.last_idx[k0:k1] if r0 == 0 else m.last_idx[k0:k1] - r0)
+        return StepMeta(ids=m.ids[r0:r1], pos=m.pos[r0:r1], slot=m.slot[r0:r1], block_tables=m.block_tables[k0:k1],
+                        seq_lens=m.seq_lens[k0:k1], cu_q=cu_q, last_idx=last,
+                        max_q_len=max(cu[i + 1] - cu[i] for i in range(k0, k1)), decode=False,
+                        cu_host=[c - r0 for c in cu[k0:k1 + 1]])
+
+    def forward(self, m: StepMeta, bufs: Optional[dict] = None) -> torch.Tensor:
+        """Run all layers and the LM head; returns next-token ids [S] (int32, greedy)."""
+        w = self.w
+        bufs = {} if bufs is None else bufs
+        T = m.ids.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"step of {T} tokens exceeds runner capacity {self.max_tokens}")
+
+        def mkbuf(store):
+            def buf(name, shape, dtype=torch.bfloat16):
+                key = (name, tuple(shape), dtype)
+                t = store.get(key)
+                if t is None:
+                    t = store[key] = torch.empty(shape, dtype=dtype, device=self.device)
+                return t
+            return buf
+
+        buf = mkbuf(bufs)
+        rng = _nvtx_range
+        k = self._split_point(m)
+        if k:
+            # two halves on two streams, layer by layer, each with its own symmetric workspace
+            self.split_steps += 1
+            halves = [(self._sub_meta(m, 0, k), self.symm, {}),
+                      (self._sub_meta(m, k, len(m.cu_host) - 1), self.symm2, {})]
+            main = torch.cuda.current_stream(self.device)
+            states = []
+            for (hm, sy, hb), st in zip(halves, self._streams):
+                st.wait_stream(main)
+                with torch.cuda.stream(st):
+                    r, n = self._resid_normed(hm.ids.shape[0], sy)
+                    self._embed(hm, r, n)
+                    states.append((hm, sy, hb, st, r, n, self._scratch(hm.ids.shape[0], mkbuf(hb))))
+            for li in range(len(w.layers)):
+                rng(f"layer {li}")
+                for hm, sy, hb, st, r, n, scr in states:
+                    with torch.cuda.stream(st):
+                        self._layer(li, hm, r, n, scr, hb, sy)
+                rng(None)
+            for state in states:
+                main.wait_stream(state[3])
+            rng("lm_head")
+            S = m.last_idx.shape[0]
+            final = buf("final", (S, self.H))
+            sa = states[0][0].last_idx.shape[0]
+            torch.index_select(states[0][5], 0, states[0][0].last_idx, out=final[:sa])
+            torch.index_select(states[1][5], 0, states[1][0].last_idx, out=final[sa:])
+            return self._lm_head(m, final, S, buf, rng)
+
+        resid, normed = self._resid_normed(T)
+        self._embed(m, resid, normed)
+        scr = self._scratch(T, buf)
+        for li in range(len(w.layers)):
             rng(f"layer {li}")
-            kc, vc = self.kv.k[li], self.kv.v[li]
-            ops.qkv_rope(normed, L.wqkv, m.pos, m.slot, self.cos, self.sin, q, kc, vc, self.hq, self.hkv,
-                         qkv_buf=qkv)
-            if m.decode:
-                ops.attn_decode(q, kc, vc, m.block_tables, m.seq_lens, attn, self.scale, self.window,
-                                max_len_hint=m.max_q_len)
-            else:
-                ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
-                                 self.window)
-            self._proj_reduce(attn, L.wo, resid, normed, L.mlp_norm, parity, bufs)
-            parity ^= 1
-            ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
-            gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
-            self._proj_reduce(h, L.wdown, resid, normed, gamma, parity, bufs)
-            parity ^= 1
+            self._layer(li, m, resid, normed, scr, bufs)
             rng(None)
 
         rng("lm_head")
@@ -256,6 +353,10 @@ class LlamaRunner:
             torch.index_select(normed, 0, m.last_idx, out=final)
         else:
             final, S = normed, T
+        return self._lm_head(m, final, S, buf, rng)
+
+    def _lm_head(self, m: StepMeta, final: torch.Tensor, S: int, buf, rng) -> torch.Tensor:
+        w = self.w
         cand = buf("cand", (S, 2), torch.float32)
         sampled = m.inv_t is not None
         if self.keep_logits or sampled or S > ops.SWAP_AB_MAX_TOKENS:

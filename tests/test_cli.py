@@ -33,6 +33,8 @@ def test_cli_device_ring_job_ledger_pool(tmp_path, monkeypatch, capsys):
         assert cli.main(["device", "init", "-n", net, "-c", url, "--preferred-provider", "cpu",
                          "--device-id", "dev-a"]) == 0
         assert (tmp_path / "device.toml").exists()
+        dev = cli.load_device()  # the control plane issued a certificate for this device's key
+        assert dev["certificate"] and dev["control_plane_public_key"] == cp.keypair.public_key().hex()
         assert cli.main(["resource", "lock", "-m", "2G"]) == 0
         assert cli.main(["ring", "join", "-m", "tiny"]) == 0
         capsys.readouterr()

@@ -497,3 +497,54 @@ def test_provider_contract_runtime_consistency():
     assert not BackendContractDescriptor.for_provider("cpu").supports_device_sampling
     with pytest.raises(ValueError):
         BackendContractDescriptor.for_provider("rocm")
+
+
+# --------------------------------------------------------------------------- device certificates
+def test_certificate_issue_verify_tamper_and_expiry(tmp_path):
+    import datetime
+    import cbor2
+    from mesh_b200.control_plane.certificate import CertificateError, ControlPlaneKeypair, verify_certificate
+    kp = ControlPlaneKeypair.load_or_generate(tmp_path / "cp.key")
+    assert ControlPlaneKeypair.load_or_generate(tmp_path / "cp.key").public_key() == kp.public_key()  # persisted
+    pk = bytes(range(32))
+    t0 = datetime.datetime(2026, 1, 1, tzinfo=datetime.timezone.utc)
+    blob = kp.generate_certificate("dev-1", "net-1", pk, now=t0)
+    cert = kp.verify_certificate(blob)
+    assert (cert.device_id, cert.network_id, cert.public_key) == ("dev-1", "net-1", pk)
+    assert cert.issued_at == "2026-01-01T00:00:00Z" and cert.expires_at == "2026-01-31T00:00:00Z"
+    assert not cert.expired(t0 + datetime.timedelta(days=29)) and cert.expired(t0 + datetime.timedelta(days=30))
+    outer = cbor2.loads(blob)
+    inner = cbor2.loads(outer["certificate"])
+    inner["device_id"] = "dev-2"
+    forged = cbor2.dumps({"certificate": cbor2.dumps(inner), "signature": outer["signature"]})
+    with pytest.raises(CertificateError):
+        kp.verify_certificate(forged)
+    with pytest.raises(CertificateError):
+        verify_certificate(blob, ControlPlaneKeypair.generate().public_key())
+    with pytest.raises(CertificateError):
+        kp.generate_certificate("d", "n", b"short")
+    with pytest.raises(CertificateError):
+        kp.verify_certificate(b"\x00garbage")
+
+
+def test_registration_issues_certificate_and_validates_inputs():
+    from mesh_b200.control_plane.certificate import verify_certificate
+    from mesh_b200.control_plane.db import Database
+    from mesh_b200.control_plane.service import ApiError, ControlPlane, NotFound
+    cp = ControlPlane(Database())
+    net = cp.create_network("lan")["network_id"]
+    pk = "ab" * 32
+    r = cp.register_device("dev-a", net, public_key=pk)
+    cert = verify_certificate(bytes.fromhex(r["certificate"]), bytes.fromhex(r["control_plane_public_key"]))
+    assert cert.device_id == "dev-a" and cert.network_id == net and cert.public_key.hex() == pk
+    stored = cp.db.query("SELECT certificate, public_key FROM devices WHERE device_id=?", ("dev-a",))[0]
+    assert stored["certificate"] == r["certificate"] and stored["public_key"] == pk
+    assert cp.register_device("dev-b", net)["certificate"] == ""  # no key, no certificate
+    with pytest.raises(ApiError):
+        cp.register_device("dev-c", net, public_key="ab" * 31)
+    with pytest.raises(ApiError):
+        cp.register_device("dev-c", net, public_key="zz" * 32)
+    with pytest.raises(ApiError):
+        cp.register_device("", net)
+    with pytest.raises(NotFound):
+        cp.register_device("dev-d", "no-such-network")

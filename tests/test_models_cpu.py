@@ -87,3 +87,30 @@ def test_artifacts_roundtrip_and_validation(tmp_path):
     p.write_bytes(bytes(b))
     with pytest.raises(artifacts.ArtifactError):
         artifacts.load_shard(out, a)
+
+
+def test_prefill_split_point_and_sub_meta():
+    """The overlapped-prefill split: the prompt boundary nearest half the tokens with both halves of
+    at least 512 tokens, and sub-steps whose rows, tables and offsets are rebased."""
+    import types
+    import torch
+    from mesh_b200.models.llama import LlamaRunner, StepMeta
+    cu = [0, 300, 580, 890, 1180, 1310]
+    T, S = cu[-1], len(cu) - 1
+    m = StepMeta(ids=torch.arange(T, dtype=torch.int32), pos=torch.arange(T, dtype=torch.int32),
+                 slot=torch.arange(T, dtype=torch.int64), block_tables=torch.arange(S * 4, dtype=torch.int32).view(S, 4),
+                 seq_lens=torch.tensor([cu[i + 1] - cu[i] for i in range(S)], dtype=torch.int32),
+                 cu_q=torch.tensor(cu, dtype=torch.int32), last_idx=torch.tensor(cu[1:], dtype=torch.int64) - 1,
+                 max_q_len=310, decode=False, cu_host=cu)
+    on = types.SimpleNamespace(overlap_prefill=True)
+    assert LlamaRunner._split_point(on, m) == 2
+    assert LlamaRunner._split_point(types.SimpleNamespace(overlap_prefill=False), m) == 0
+    small = StepMeta(ids=m.ids[:600], pos=m.pos, slot=m.slot, block_tables=m.block_tables, seq_lens=m.seq_lens,
+                     decode=False, cu_host=[0, 300, 600])
+    assert LlamaRunner._split_point(on, small) == 0  # halves under 512 tokens
+    a, b = LlamaRunner._sub_meta(m, 0, 2), LlamaRunner._sub_meta(m, 2, S)
+    assert a.ids.shape[0] == 580 and b.ids.shape[0] == 730 and int(b.ids[0]) == 580
+    assert b.cu_q.tolist() == [0, 310, 600, 730] and b.cu_host == [0, 310, 600, 730]
+    assert b.last_idx.tolist() == [309, 599, 729] and a.last_idx.tolist() == [299, 579]
+    assert b.block_tables.tolist() == m.block_tables[2:].tolist() and b.max_q_len == 310 and a.max_q_len == 300
+    assert not a.decode and not b.decode

@@ -421,6 +421,39 @@ def test_allreduce_bounded_wait_reports_timeout_2gpu():
     _run(_timeout_check, 2)
 
 
+def _overlap_check(rank, world):
+    """Prefill chunks of several prompts run as two overlapped halves (two streams, two symmetric
+    workspaces) and as one piece: the generated tokens are bitwise the same, and halves ran."""
+    import torch.distributed as dist
+    from mesh_b200 import ops
+    from mesh_b200.config import EngineConfig, get_preset
+    from mesh_b200.engine.serving import Engine
+    from mesh_b200.models.llama import KVPool, LlamaRunner
+    from mesh_b200.models.weights import synthetic_device_weights
+    dev = torch.device("cuda", rank)
+    cfg = get_preset("small")
+    gen = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (300, 280, 310, 290, 130)]
+    out = {}
+    for overlap in (False, True):
+        ecfg = EngineConfig(max_seq_len=512, prefill_chunk_tokens=2048, prefill_overlap=overlap, tp=world)
+        w = synthetic_device_weights(cfg, rank, world, seed=21, device=dev, norm_noise=True)
+        kv = KVPool(cfg, w.layout.local_kv_heads, 256, 16, dev)
+        r = LlamaRunner(w, ecfg, kv, dev, group=dist.group.WORLD, max_tokens=2048)
+        eng = Engine(r, ecfg, max_batch=8)
+        out[overlap] = eng.generate(prompts, 6)
+        torch.cuda.synchronize()
+        ops.scratch(dev).check("overlap")
+        assert r.overlap_prefill == overlap and (r.split_steps > 0) == overlap, (overlap, r.split_steps)
+        eng.close()
+    assert out[True] == out[False]
+
+
+def test_prefill_overlap_halves_equal_whole_2gpu():
+    _need(2)
+    _run(_overlap_check, 2)
+
+
 @pytest.mark.parametrize("ar", ["auto", "gemm_ar"])
 def test_tp2_logits_match_tp1(ar):
     _need(2)
