@@ -29,7 +29,8 @@ void attn_decode(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor
 int64_t attn_decode_pick_splits(int64_t B, int64_t hkv, int64_t max_len, int64_t num_sms);
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
                     const at::Tensor& block_tables, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& ws,
-                    at::Tensor& err, int64_t splits, double scale, int64_t window);
+                    at::Tensor& err, int64_t splits, double scale, int64_t window,
+                    const c10::optional<at::Tensor>& counters);
 void attn_prefill(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache, const at::Tensor& cu_q,
                   const at::Tensor& k_lens, const at::Tensor& block_tables, at::Tensor& out, int64_t max_q_len,
                   double scale, int64_t window);
@@ -86,7 +87,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_merge", &mesh::argmax_merge, "merge per-rank argmax candidates");
   m.def("argmax_tiles", &mesh::argmax_tiles, "reduce LM-head per-tile argmax candidates");
   m.def("attn_decode", &mesh::attn_decode, "paged GQA decode attention (split-KV)");
-  m.def("attn_decode_tc", &mesh::attn_decode_tc, "paged GQA decode attention, TMA-streamed tensor-core variant");
+  m.def("attn_decode_tc", &mesh::attn_decode_tc, "paged GQA decode attention, TMA-streamed tensor-core variant",
+        py::arg("q"), py::arg("kcache"), py::arg("vcache"), py::arg("block_tables"), py::arg("seq_lens"),
+        py::arg("out"), py::arg("ws"), py::arg("err"), py::arg("splits"), py::arg("scale"), py::arg("window"),
+        py::arg("counters") = py::none());
   m.def("attn_decode_pick_splits", &mesh::attn_decode_pick_splits, "split-KV heuristic");
   m.def("attn_prefill", &mesh::attn_prefill, "paged causal varlen GQA prefill attention");
   m.def("attn_prefill_tc", &mesh::attn_prefill_tc,

@@ -65,7 +65,8 @@ void attn_decode(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor
 // TMA-streamed tensor-core variant (head_dim 128, 16-token pages).
 void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
                     const at::Tensor& block_tables, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& ws,
-                    at::Tensor& err, int64_t splits, double scale, int64_t window) {
+                    at::Tensor& err, int64_t splits, double scale, int64_t window,
+                    const c10::optional<at::Tensor>& counters) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous(), "attn_decode_tc: q bf16 [B, hq*D]");
   TORCH_CHECK(kcache.dim() == 4 && kcache.sizes() == vcache.sizes() && kcache.is_contiguous() && vcache.is_contiguous(),
               "attn_decode_tc: cache [pages, hkv, 16, 128] contiguous");
@@ -94,6 +95,13 @@ void attn_decode_tc(const at::Tensor& q, const at::Tensor& kcache, const at::Ten
   a.splits = (int)splits;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.window = (int)window;
+  a.counters = nullptr;
+  if (splits > 1 && counters.has_value() && counters->defined() && counters->numel() > 0) {
+    TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kInt && counters->is_contiguous() &&
+                    counters->numel() >= (int64_t)B * hkv,
+                "attn_decode_tc: counters int32 [>= B * hkv], zero between launches");
+    a.counters = counters->data_ptr<int>();
+  }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (G) {
     case 1: launch_attn_decode_tc_g<1>(tk, tv, a, B, st); break;

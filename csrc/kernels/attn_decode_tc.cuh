@@ -36,6 +36,10 @@ struct DecodeTcArgs {
   int max_pages, hkv, splits;
   float scale_log2;
   int window;
+  // split > 1: per-(sequence, KV head) arrival counters (zero between launches). When set, the
+  // last split CTA of a (sequence, KV head) merges the partials itself and resets its counter, so
+  // no separate combine launch follows; null keeps the combine kernel.
+  int* counters;
 };
 
 __device__ __forceinline__ void dtc_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -277,6 +281,36 @@ __global__ void __launch_bounds__(160) attn_decode_tc_kernel(const __grid_consta
         if (d == 0) w[D] = lsum > 0.f ? M + log2f(lsum) : -INFINITY;
       }
     }
+    if (a.splits > 1 && a.counters != nullptr) {
+      // threadfence-reduction: publish this split's partial, count it, and let the last arrival
+      // merge all splits (same arithmetic and order as attn_decode_combine_kernel)
+      __shared__ int s_last;
+      __threadfence();
+      named_bar_sync(1, 128);
+      int* cnt = a.counters + (long)seq * a.hkv + h;
+      if (threadIdx.x == 0) s_last = (atomicAdd(cnt, 1) == a.splits - 1) ? 1 : 0;
+      named_bar_sync(1, 128);
+      if (s_last) {
+        __threadfence();
+        for (int i = threadIdx.x; i < G * D; i += 128) {
+          const int g = i / D, d = i - g * D;
+          const int qh = h * G + g;
+          const float* w = a.ws + ((long)seq * hq + qh) * a.splits * (D + 1);
+          float M = -INFINITY;
+          for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, __ldcg(w + sp * (D + 1) + D));
+          float num = 0.f, den = 0.f;
+          if (M != -INFINITY) {
+            for (int sp = 0; sp < a.splits; ++sp) {
+              const float f = exp2f(__ldcg(w + sp * (D + 1) + D) - M);
+              num += __ldcg(w + sp * (D + 1) + d) * f;
+              den += f;
+            }
+          }
+          a.out[(long)seq * hq * D + qh * D + d] = f2bf(den > 0.f ? num / den : 0.f);
+        }
+        if (threadIdx.x == 0) *cnt = 0;  // ready for the next launch
+      }
+    }
   }
 }
 
@@ -294,7 +328,7 @@ inline void launch_attn_decode_tc_g(const CUtensorMap& tk, const CUtensorMap& tv
     configured[dev] = true;
   }
   C10_CUDA_CHECK(launch_k(kern, dim3(B, a.hkv, a.splits), dim3(160), attn_decode_tc_smem(), st, tk, tv, a));
-  if (a.splits > 1)
+  if (a.splits > 1 && a.counters == nullptr)
     C10_CUDA_CHECK(launch_k(attn_decode_combine_kernel<128>, dim3(B, a.hkv * G), dim3(128), 0, st,
                             (const float*)a.ws, a.out, a.hkv * G, a.splits));
 }

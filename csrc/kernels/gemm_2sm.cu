@@ -400,15 +400,16 @@ void gemm_2sm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t
   p.K = K;
   p.ldo = out.stride(0);
   p.m_tiles = (M + TM - 1) / TM;
-  // tile width: 256 columns. 128-column tiles (argument or MESH_PAIR_TN=128) fill a short last
-  // wave better but move half again as many operand bytes per FLOP and measured 37-46 % slower;
-  // 512-column tiles (argument or MESH_PAIR_TN=512) move a quarter fewer.
+  // tile width: 128-column tiles (argument or MESH_PAIR_TN=128) fill a short last wave better but
+  // move half again as many operand bytes per FLOP and measured 37-46 % slower than 256.
   static const int force_tn = [] {
     const char* e = std::getenv("MESH_PAIR_TN");
     return e ? std::atoi(e) : 0;
   }();
   auto valid_tn = [&](int v) { return (v == 128 || v == 256 || v == 512) && !(v == 128 && epi == SILU_BF16); };
-  int tn_sel = 256;
+  // default: 512-column tiles wherever N fills them (measured 1.35-1.51 PFLOP/s on the Llama-3-8B
+  // prefill shapes at T=4096 against 1.19-1.30 with 256 columns)
+  int tn_sel = N >= 1024 ? 512 : 256;
   if (valid_tn((int)tn))
     tn_sel = (int)tn;
   else if (valid_tn(force_tn))

@@ -67,6 +67,8 @@ class DeviceScratch:
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=self.device)
         self.gemm_counters = torch.zeros(4096, dtype=torch.int32, device=self.device)
         self.attn_ws = torch.empty(0, dtype=torch.float32, device=self.device)
+        # split decode attention: per-(sequence, KV head) arrival counters, zero between launches
+        self.attn_cnt = torch.zeros(0, dtype=torch.int32, device=self.device)
         props = torch.cuda.get_device_properties(self.device)
         self.num_sms = props.multi_processor_count
 
@@ -78,16 +80,21 @@ class DeviceScratch:
         if self.gemm_counters.numel() < tiles:
             self.gemm_counters = torch.zeros(tiles * 2, dtype=torch.int32, device=self.device)
 
-    def ensure_attn(self, floats: int):
+    def ensure_attn(self, floats: int, counters: int = 0):
         if self.attn_ws.numel() < floats:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("attention scratch must be sized before CUDA graph capture")
             self.attn_ws = torch.empty(max(floats, 1 << 20), dtype=torch.float32, device=self.device)
+        if self.attn_cnt.numel() < counters:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("attention scratch must be sized before CUDA graph capture")
+            self.attn_cnt = torch.zeros(max(counters, 4096), dtype=torch.int32, device=self.device)
 
     def check(self, what: str = "kernel"):
         v = int(self.err.item())
         if v:
             self.err.zero_()
+            self.attn_cnt.zero_()  # a launch that unwound early may have left counts behind
             raise RuntimeError(f"{what}: device error code {v} (1-3 pipeline wait timeout, 4 peer timeout, 5 bad argument)")
 
 
@@ -172,8 +179,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     return gemm(x, w, out, epi, trans=False, push=push)
 
 
-# Prefill-sized products run on SM pairs (256x256 tiles, tcgen05.mma.cta_group::2) from this many
-# tokens: 1.18-1.31 PFLOP/s on the Llama-3-8B prefill shapes at T=4096 against 1.04-1.25 for the
+# Prefill-sized products run on SM pairs (256x512 tiles, tcgen05.mma.cta_group::2) from this many
+# tokens: 1.34-1.51 PFLOP/s on the Llama-3-8B prefill shapes at T=4096 against 1.04-1.25 for the
 # one-SM kernel. MESH_PAIR_GEMM=0 keeps the one-SM kernel everywhere (A/B measurements).
 PAIR_GEMM_MIN_TOKENS = 512
 _PAIR_GEMM = os.environ.get("MESH_PAIR_GEMM", "1") != "0"
@@ -184,7 +191,7 @@ def gemm_pair(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EP
     """out = x @ w.T (EPI_SILU_BF16: SiLU(gate) * up of the interleaved gate/up product) on SM pairs.
     trace: optional int64 [384] of %globaltimer stamps for the first pair (producer empty-waits of both
     CTAs, then the MMA thread's full-waits). tn: tile width (128, 256 or 512 output columns per SM
-    pair; 0: the default, 256, or ``MESH_PAIR_TN``)."""
+    pair; 0: ``MESH_PAIR_TN`` if set, else 512 from N >= 1024 and 256 below)."""
     if tn:
         ext().gemm_2sm(x, w, out, epi, scratch(x.device).err, trace, tn)
     else:
@@ -248,6 +255,11 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
     return out
 
 
+# split decode attention merges its partials in the last CTA of each (sequence, KV head) instead of a
+# separate combine launch; MESH_ATTN_FUSED_COMBINE=0 restores the combine kernel (A/B measurements)
+_FUSED_COMBINE = os.environ.get("MESH_ATTN_FUSED_COMBINE", "1") != "0"
+
+
 def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, window: int = 0,
                 splits: int = 0, max_len_hint: int = 0, impl: str = "auto"):
     """Paged GQA decode attention. impl: "tc" (TMA-streamed, tensor-core fragments; head_dim 128,
@@ -259,13 +271,15 @@ def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, wi
         impl = "tc" if (D == 128 and ps == 16) else "simt"
     if splits <= 0:
         splits = ext().attn_decode_pick_splits(B, hkv, max_len_hint or block_tables.shape[1] * ps, s.num_sms)
+    fused = impl == "tc" and _FUSED_COMBINE
     if splits > 1:
-        s.ensure_attn(B * hq * splits * (D + 1))
+        s.ensure_attn(B * hq * splits * (D + 1), B * hkv if fused else 0)
     if impl == "tc":
-        ext().attn_decode_tc(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, s.err, splits, scale, window)
+        ext().attn_decode_tc(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, s.err, splits, scale, window,
+                             s.attn_cnt if (fused and splits > 1) else None)
     else:
         ext().attn_decode(q, kcache, vcache, block_tables, seq_lens, out, s.attn_ws, splits, scale, window)
-    _count(2 if splits > 1 else 1)
+    _count(2 if (splits > 1 and not fused) else 1)
     return out
 
 

@@ -323,6 +323,28 @@ def test_attn_decode(G, D, impl, splits, window):
         assert rel_err(out[i].view(1, hq, D), want) < 2e-2, (i, L)
 
 
+@pytest.mark.parametrize("splits", [2, 5])
+def test_attn_decode_in_kernel_combine(splits, monkeypatch):
+    """Split decode attention merging its partials in the last CTA of each (sequence, KV head):
+    bitwise equal to the separate combine kernel, the same on a repeated launch, and every arrival
+    counter back at zero afterwards."""
+    lens = [1, 17, 300, 1029, 64, 700]
+    hkv, ps, G, D = 2, 16, 4, 128
+    kc, vc, bt, ks, vs = _paged_kv(lens, hkv, D, ps, seed=21)
+    q = _rand(len(lens), hkv * G * D, seed=31)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    outs = []
+    for fused in (True, True, False):
+        monkeypatch.setattr(ops, "_FUSED_COMBINE", fused)
+        out = torch.full_like(q, float("nan"))
+        ops.attn_decode(q, kc, vc, bt, sl, out, 1 / math.sqrt(D), 0, splits=splits, impl="tc")
+        torch.cuda.synchronize()
+        outs.append(out)
+    ops.scratch(DEV).check("attn_decode")
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert int(ops.scratch(DEV).attn_cnt.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("G", [4, 8, 1, 2])
 @pytest.mark.parametrize("window", [0, 50])
 @pytest.mark.parametrize("impl", ["tc", "fa2"])
