@@ -3,7 +3,8 @@
     mesh device init|start|runtime|status       mesh ring join|leave|status|topology|shard
     mesh resource lock|unlock|status            mesh job run|status|watch|stats
     mesh ledger summary|events                  mesh pool create|join|list|peers|status
-    mesh doctor [--stage preflight|production]  mesh ui [--api-only]
+    mesh model import-hf|reshard|list|info      mesh doctor [--stage preflight|production]
+    mesh ui [--api-only]
 
 Device state lives in ``$MESHNET_HOME`` (default ``~/.meshnet``): ``device.toml`` (identity,
 control-plane URL, ``[execution]``, ``[governance]`` and the ``[b200]`` section), an ed25519 key,
@@ -441,6 +442,32 @@ def cmd_pool(a):
         print(json.dumps({"pools": len(list(pools.glob("*.json")))}))
 
 
+# ------------------------------------------------------------------------------------------ model
+def cmd_model(a):
+    """The on-disk model store (``$MESHNET_MODEL_STORE``, default ``$MESHNET_HOME/models``) and the
+    device's shard registry: import a Hugging Face Llama checkpoint, re-shard, list, describe."""
+    from ..models.artifacts import model_store_dir
+    from ..models.registry import ModelInfo, ShardRegistry
+    store = Path(getattr(a, "store", None) or model_store_dir())
+    if a.action == "import-hf":
+        from ..models.convert import import_hf_llama
+        out = import_hf_llama(a.src, store, a.model_id, a.workers)
+        ShardRegistry(home() / "shards").register_model(ModelInfo.from_model_dir(out))
+        print(json.dumps({"model_dir": str(out)}))
+    elif a.action == "reshard":
+        from ..models.convert import reshard
+        out = reshard(store / a.model_id, Path(a.out) if a.out else store / f"{a.model_id}-tp{a.workers}", a.workers)
+        print(json.dumps({"model_dir": str(out)}))
+    elif a.action == "info":
+        from dataclasses import asdict
+        info = ModelInfo.from_model_dir(store / a.model_id, gpu_bytes=a.gpu_bytes or None)
+        print(json.dumps(asdict(info), indent=2))
+    else:
+        models = sorted(p.parent.name for p in store.glob("*/model.json")) if store.exists() else []
+        print(json.dumps({"store": str(store), "models": models,
+                          "registry": ShardRegistry(home() / "shards").summary()}, indent=2))
+
+
 # ------------------------------------------------------------------------------------------ doctor
 def cmd_doctor(a):
     checks = []
@@ -558,6 +585,24 @@ def build_parser():
     pi.set_defaults(fn=cmd_pool)
     pp.set_defaults(fn=cmd_pool)
     pool.add_parser("status").set_defaults(fn=cmd_pool)
+    mdl = sub.add_parser("model").add_subparsers(dest="action", required=True)
+    mi = mdl.add_parser("import-hf", help="import a local Hugging Face Llama checkpoint into the model store")
+    mi.add_argument("--src", required=True)
+    mi.add_argument("--model-id", required=True)
+    mi.add_argument("--workers", type=int, default=1)
+    mi.add_argument("--store")
+    mr = mdl.add_parser("reshard", help="rewrite an on-disk model for another worker count")
+    mr.add_argument("--model-id", required=True)
+    mr.add_argument("--workers", type=int, required=True)
+    mr.add_argument("--store")
+    mr.add_argument("--out")
+    mdl.add_parser("list", help="models in the store and shards in this device's registry").set_defaults(fn=cmd_model)
+    ms = mdl.add_parser("info", help="one model's description (memory per worker, valid TP degrees)")
+    ms.add_argument("--model-id", required=True)
+    ms.add_argument("--store")
+    ms.add_argument("--gpu-bytes", type=int, default=0)
+    for q in (mi, mr, ms):
+        q.set_defaults(fn=cmd_model)
     doc = sub.add_parser("doctor")
     doc.add_argument("--stage", choices=["preflight", "production"], default="production")
     doc.set_defaults(fn=cmd_doctor)

@@ -49,3 +49,23 @@ def test_reshard_roundtrip(tmp_path):
     for a, b in zip(back.layers, w.layers):
         for k in a:
             assert np.array_equal(a[k], b[k]), k
+
+
+def test_mesh_model_cli(tmp_path, monkeypatch, capsys):
+    """`mesh model import-hf | info | reshard | list` over the model store and the shard registry."""
+    from mesh_b200.cli import main as cli
+    monkeypatch.setenv("MESHNET_HOME", str(tmp_path / "home"))
+    monkeypatch.setenv("MESHNET_MODEL_STORE", str(tmp_path / "store"))
+    _tiny_hf(tmp_path / "hf")
+    assert cli.main(["model", "import-hf", "--src", str(tmp_path / "hf"), "--model-id", "tiny-hf", "--workers", "2"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert (tmp_path / "store" / "tiny-hf" / "shard-1-of-2.safetensors").exists() and out["model_dir"]
+    assert cli.main(["model", "info", "--model-id", "tiny-hf", "--gpu-bytes", str(10 ** 9)]) == 0
+    info = json.loads(capsys.readouterr().out)
+    assert info["num_layers"] == 2 and info["num_kv_heads"] == 2 and info["min_workers"] == 1
+    assert cli.main(["model", "reshard", "--model-id", "tiny-hf", "--workers", "1"]) == 0
+    re_dir = json.loads(capsys.readouterr().out)["model_dir"]
+    assert (tmp_path / "store" / "tiny-hf-tp1" / "tiny-hf" / "shard-0-of-1.safetensors").exists(), re_dir
+    assert cli.main(["model", "list"]) == 0
+    lst = json.loads(capsys.readouterr().out)
+    assert "tiny-hf" in lst["models"] and "tiny-hf" in lst["registry"]["models"]
