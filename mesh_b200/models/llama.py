@@ -127,18 +127,25 @@ class LlamaRunner:
             self.symm = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
         # Prefill overlap: a chunk of several prompts runs as two halves on two streams, each with its
         # own symmetric workspace, so one half's all-reduces (NVLink, a few SMs) run while the other
-        # half's GEMMs hold the tensor cores. Only with the peer-memory all-reduce (NCCL calls on two
-        # streams could be ordered differently on different ranks) and when both halves are big
-        # enough for the SM-pair GEMM, which uses no shared workspace.
+        # half's GEMMs hold the tensor cores. Every all-reduce goes through one third stream, in the
+        # same order on every rank: a GPU then never holds two all-reduce grids that wait on peers at
+        # once (two such grids, each waiting for blocks the peer GPU could not schedule because its
+        # SMs were held by the other one, stalled until their bounded waits ran out). Only with the
+        # peer-memory all-reduce (NCCL calls on two streams could be ordered differently on
+        # different ranks) and when both halves are big enough for the SM-pair GEMM, which uses no
+        # shared workspace.
         self.overlap_prefill = (self.use_fused_ar and not self.push_rs and bool(ecfg.prefill_overlap)
                                 and max_tokens >= 2 * PREFILL_SPLIT_MIN_TOKENS)
         self.symm2 = None
         self._streams = None
+        self._comm = None
         self.split_steps = 0
         if self.overlap_prefill:
             from ..parallel.symm import SymmWorkspace
             self.symm2 = SymmWorkspace(max_tokens, self.H, self.device, group, multicast=ecfg.nvls)
+            # two compute streams (one per half) and one stream that runs every all-reduce
             self._streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+            self._comm = torch.cuda.Stream(self.device)
         # vocabulary-parallel embedding: this rank's rows live in a table every peer maps, and each
         # token's row is read from its owner (one launch, fused with the first RMSNorm)
         self.emb_table = None
@@ -178,8 +185,16 @@ class LlamaRunner:
         return T * self.H * 2 * (self.world - 1) > (8 << 20)
 
     def _reduce(self, part: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor, gamma: torch.Tensor,
-                parity: int, symm=None):
-        """resid += sum_ranks(part); normed = RMSNorm(resid) * gamma."""
+                parity: int, symm=None, comm=None):
+        """resid += sum_ranks(part); normed = RMSNorm(resid) * gamma. With ``comm`` the all-reduce
+        runs on that stream, ordered after the current stream's work and before its next."""
+        if comm is not None:
+            cur = torch.cuda.current_stream(self.device)
+            comm.wait_stream(cur)
+            with torch.cuda.stream(comm):
+                self._reduce(part, resid, normed, gamma, parity, symm, comm)
+            cur.wait_stream(comm)
+            return
         T = resid.shape[0]
         eps = self.cfg.rms_norm_eps
         symm = symm or self.symm
@@ -206,7 +221,7 @@ class LlamaRunner:
         return scratch[key]
 
     def _proj_reduce(self, x: torch.Tensor, wt: torch.Tensor, resid: torch.Tensor, normed: torch.Tensor,
-                     gamma: torch.Tensor, parity: int, bufs: dict, symm=None):
+                     gamma: torch.Tensor, parity: int, bufs: dict, symm=None, comm=None):
         """resid += sum_ranks(x @ wt.T); normed = RMSNorm(resid) * gamma (row-parallel projection)."""
         T = x.shape[0]
         if self.gemm_ar and T <= ops.SWAP_AB_MAX_TOKENS:
@@ -215,7 +230,7 @@ class LlamaRunner:
             return
         part = self._part_buf(T, parity, bufs, symm)
         ops.linear(x, wt, out=part, push=self._push(T, parity))
-        self._reduce(part, resid, normed, gamma, parity, symm)
+        self._reduce(part, resid, normed, gamma, parity, symm, comm)
 
     # ------------------------------------------------------------------------------------------
     def _embed(self, m: StepMeta, resid: torch.Tensor, normed: torch.Tensor) -> None:
@@ -240,7 +255,7 @@ class LlamaRunner:
                 t.fill_(float("nan"))
         return qkv, q, attn, h
 
-    def _layer(self, li: int, m: StepMeta, resid, normed, scr: tuple, bufs: dict, symm=None) -> None:
+    def _layer(self, li: int, m: StepMeta, resid, normed, scr: tuple, bufs: dict, symm=None, comm=None) -> None:
         """One decoder layer; ``normed`` holds this layer's attention-normed input on entry and the
         next layer's (or the final norm's) on exit. Each layer runs two all-reduces, so the
         partial-buffer parity is the same (0 then 1) in every layer."""
@@ -255,10 +270,10 @@ class LlamaRunner:
         else:
             ops.attn_prefill(q, kc, vc, m.cu_q, m.seq_lens, m.block_tables, attn, m.max_q_len, self.scale,
                              self.window)
-        self._proj_reduce(attn, L.wo, resid, normed, L.mlp_norm, 0, bufs, symm)
+        self._proj_reduce(attn, L.wo, resid, normed, L.mlp_norm, 0, bufs, symm, comm)
         ops.linear(normed, L.wgu, out=h, epi=ops.EPI_SILU_BF16)
         gamma = w.layers[li + 1].attn_norm if li + 1 < len(w.layers) else w.final_norm
-        self._proj_reduce(h, L.wdown, resid, normed, gamma, 1, bufs, symm)
+        self._proj_reduce(h, L.wdown, resid, normed, gamma, 1, bufs, symm, comm)
 
     def _split_point(self, m: StepMeta) -> int:
         """Number of prompts in the first half of a prefill chunk run as two overlapped halves, or 0
@@ -326,7 +341,7 @@ class LlamaRunner:
                 rng(f"layer {li}")
                 for hm, sy, hb, st, r, n, scr in states:
                     with torch.cuda.stream(st):
-                        self._layer(li, hm, r, n, scr, hb, sy)
+                        self._layer(li, hm, r, n, scr, hb, sy, self._comm)
                 rng(None)
             for state in states:
                 main.wait_stream(state[3])
