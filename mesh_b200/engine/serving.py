@@ -18,7 +18,6 @@ B200 specifics:
 """
 from __future__ import annotations
 
-import math
 import time
 from collections import deque
 from dataclasses import dataclass, field
@@ -28,7 +27,7 @@ import numpy as np
 import torch
 
 from ..config import EngineConfig, ModelConfig
-from ..models.llama import KVPool, LlamaRunner, StepMeta
+from ..models.llama import LlamaRunner, StepMeta
 from .pages import PageAllocator
 
 

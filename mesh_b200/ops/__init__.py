@@ -8,7 +8,6 @@ from __future__ import annotations
 
 import os
 
-import math
 import threading
 from typing import Optional
 
