@@ -205,6 +205,48 @@ def attnprefill(args):
         del kc, vc, q, out
 
 
+# ------------------------------------------------------------------------------------ decode GEMM schedules
+def decodemodes(args):
+    """The four decode GEMMs of one TP rank (swap-AB, T tokens) under each schedule the tcgen05 GEMM
+    has (0 = the planner's automatic choice, 1 = whole tiles, 2 = stream-K, 3 = cluster split-K),
+    against cuBLAS on the same product; CUDA-graph timed with the weights rotated past L2. Shows
+    whether the automatic choice is the fastest at a TP degree's shapes."""
+    import torch
+    from . import ops
+    from .config import get_preset
+    from .models.sharding import shard_layout
+    from .models.weights import GU_BLOCK, pad_to
+    from .utils.opbench import copies_for, timeit
+    cfg = get_preset(args.model)
+    lay = shard_layout(cfg, 0, args.tp)
+    H, D, T = cfg.hidden_dim, cfg.head_dim, args.tokens
+    i_loc = lay.mlp_cols
+    shapes = {"qkv": ((lay.local_q_heads + 2 * lay.local_kv_heads) * D, H, ops.EPI_STORE_BF16),
+              "o_proj": (H, lay.local_q_heads * D, ops.EPI_STORE_BF16),
+              "gate_up": (2 * pad_to(i_loc, GU_BLOCK), H, ops.EPI_SILU_BF16),
+              "down": (H, pad_to(i_loc, GU_BLOCK), ops.EPI_STORE_BF16)}
+    dev = torch.device("cuda", 0)
+    x_all = torch.randn(T, max(H, 8 * 4096), device=dev).to(torch.bfloat16)
+    for name, (N, K, epi) in shapes.items():
+        nc = min(copies_for(N * K * 2), 64)
+        ws = [torch.randn(N, K, device=dev).mul_(0.02).to(torch.bfloat16) for _ in range(nc)]
+        x = x_all[:, :K].contiguous()
+        n_out = N // 2 if epi == ops.EPI_SILU_BF16 else N
+        out = torch.empty(T, n_out, device=dev, dtype=torch.bfloat16)
+        row = {"tp": args.tp, "op": name, "N": N, "K": K, "T": T,
+               "plan": list(ops.ext().gemm_plan(N, T, K, epi, True, 0))}
+        for mode in args.modes:
+            try:
+                row[f"mode{mode}_us"] = round(timeit(lambda i: ops.gemm(ws[i % nc], x, out, epi, trans=True, mode=mode)), 2)
+            except RuntimeError as e:
+                row[f"mode{mode}_us"] = f"n/a ({str(e)[:60]})"
+        ref = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+        row["cublas_us"] = round(timeit(lambda i: torch.mm(x, ws[i % nc].t(), out=ref)), 2)
+        ops.scratch(dev).check("decodemodes")
+        print(json.dumps(row), flush=True)
+        del ws
+
+
 # ------------------------------------------------------------------------------------ prefill GEMM kernels
 def gemmcmp(args):
     """One prefill-sized product out = A @ B^T on one GPU: the SM-pair kernel, the one-SM kernel and
@@ -555,6 +597,11 @@ def main():
     c7.add_argument("--tp", type=int, default=1)
     c7.add_argument("--impls", nargs="+", default=["tc", "fa2"])
     c7.add_argument("--no-sdpa", action="store_true")
+    c9 = sub.add_parser("decodemodes")
+    c9.add_argument("--model", default="llama3-8b")
+    c9.add_argument("--tp", type=int, default=8)
+    c9.add_argument("--tokens", type=int, default=64)
+    c9.add_argument("--modes", type=int, nargs="+", default=[0, 1, 2, 3])
     c8 = sub.add_parser("gemmcmp")
     c8.add_argument("--M", type=int, default=4096)
     c8.add_argument("--N", type=int, default=4096)
@@ -579,7 +626,7 @@ def main():
     c4.add_argument("--layers", type=int, default=0)
     a = ap.parse_args()
     {"cpu-tp2": cpu_tp2, "prefill": prefill, "allreduce": allreduce, "serve70b": serve70b,
-     "gemmar": gemmar, "attnprefill": attnprefill, "gemmcmp": gemmcmp}[a.cmd](a)
+     "gemmar": gemmar, "attnprefill": attnprefill, "gemmcmp": gemmcmp, "decodemodes": decodemodes}[a.cmd](a)
 
 
 if __name__ == "__main__":
