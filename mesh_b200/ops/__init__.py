@@ -254,9 +254,11 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor):
     return out
 
 
-# split decode attention merges its partials in the last CTA of each (sequence, KV head) instead of a
-# separate combine launch; MESH_ATTN_FUSED_COMBINE=0 restores the combine kernel (A/B measurements)
-_FUSED_COMBINE = os.environ.get("MESH_ATTN_FUSED_COMBINE", "1") != "0"
+# MESH_ATTN_FUSED_COMBINE=1: split decode attention merges its partials in the last CTA of each
+# (sequence, KV head) instead of a separate combine launch. Measured at the TP8 decode shape (64 x 576
+# keys, 1 KV head) it took 13.0 us against 8.9 us for the split kernel plus the combine launch (every
+# CTA's device-wide fence and the serial merge cost more than the launch they save), so it is off.
+_FUSED_COMBINE = os.environ.get("MESH_ATTN_FUSED_COMBINE", "0") == "1"
 
 
 def attn_decode(q, kcache, vcache, block_tables, seq_lens, out, scale: float, window: int = 0,
